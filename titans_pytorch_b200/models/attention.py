@@ -1,0 +1,158 @@
+"""Attention modules: RoPE, sliding-window attention (MAG/MAL), segmented attention (MAC).
+
+Public surface and parameter names follow the reference
+(`src/titans/attention.py:23-441`): ``proj_q/k/v/out`` (no bias, N(0, init_std)),
+``rope.inv_freq`` (persistent buffer).  The compute is one kernel,
+:func:`titans_pytorch_b200.ops.attention.window_attention`, which replaces the
+reference's dense additive mask + SDPA with a windowed flash kernel that skips
+masked tiles, applies RoPE on load, and for MAC never computes the prefix
+query rows whose outputs the reference discards (`attention.py:424`).
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from ..config import TitansConfig
+from ..ops.attention import prefix_window_mask, window_attention
+
+
+class RotaryPositionEmbedding(nn.Module):
+    """Interleaved-pair rotary embedding, base 10000 (RoFormer)."""
+
+    def __init__(self, dim: int, max_seq_len: int = 8192, base: float = 10000.0) -> None:
+        super().__init__()
+        self.dim = dim
+        self.max_seq_len = max_seq_len
+        self.base = base
+        inv_freq = 1.0 / (base ** (torch.arange(0, dim, 2).float() / dim))
+        self.register_buffer("inv_freq", inv_freq)
+        self._build_cache(max_seq_len)
+
+    def _build_cache(self, seq_len: int, device=None, dtype=None) -> None:
+        inv = self.inv_freq if device is None else self.inv_freq.to(device)
+        ang = torch.outer(torch.arange(seq_len, device=inv.device, dtype=torch.float32), inv.float())
+        cos, sin = ang.cos(), ang.sin()
+        if dtype is not None:
+            cos, sin = cos.to(dtype), sin.to(dtype)
+        self.register_buffer("cos_cached", cos, persistent=False)
+        self.register_buffer("sin_cached", sin, persistent=False)
+        self._cache_key = (device, dtype)
+
+    def forward(self, q: torch.Tensor, k: torch.Tensor, seq_offset: int = 0):
+        """Rotate ``q`` and ``k`` ([B, H, S, d]) at positions seq_offset.. ."""
+        n = q.shape[2]
+        if (seq_offset + n > self.cos_cached.shape[0]
+                or self._cache_key != (q.device, q.dtype)):
+            self._build_cache(max(seq_offset + n, self.max_seq_len), q.device, q.dtype)
+        cos = self.cos_cached[seq_offset:seq_offset + n]
+        sin = self.sin_cached[seq_offset:seq_offset + n]
+        return self._apply_rotary(q, cos, sin), self._apply_rotary(k, cos, sin)
+
+    @staticmethod
+    def _apply_rotary(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+        a, b = x[..., 0::2], x[..., 1::2]
+        c, s = cos[None, None], sin[None, None]
+        return torch.stack([a * c - b * s, a * s + b * c], dim=-1).flatten(-2)
+
+
+class _AttentionBase(nn.Module):
+    def __init__(self, config: TitansConfig) -> None:
+        super().__init__()
+        self.config = config
+        self.dim = config.dim
+        self.num_heads = config.num_heads
+        self.head_dim = config.head_dim
+        self.scale = self.head_dim ** -0.5
+        self.use_kernels = config.use_kernels
+        self.proj_q = nn.Linear(config.dim, config.dim, bias=False)
+        self.proj_k = nn.Linear(config.dim, config.dim, bias=False)
+        self.proj_v = nn.Linear(config.dim, config.dim, bias=False)
+        self.proj_out = nn.Linear(config.dim, config.dim, bias=False)
+        self.rope: RotaryPositionEmbedding | None = None
+        if config.use_rope:
+            self.rope = RotaryPositionEmbedding(config.head_dim, config.max_seq_len)
+        self.dropout = nn.Dropout(config.dropout)
+        for m in (self.proj_q, self.proj_k, self.proj_v, self.proj_out):
+            nn.init.normal_(m.weight, std=config.init_std)
+
+    def _heads(self, t: torch.Tensor) -> torch.Tensor:
+        return t.view(*t.shape[:-1], self.num_heads, self.head_dim)
+
+    def _attend(self, q, k, v, pk, pv, window):
+        """q/k/v: [B, T, D]; pk/pv: [B or 1, P, D] or None -> [B, T, D] after proj_out."""
+        o = window_attention(
+            self._heads(q), self._heads(k), self._heads(v),
+            None if pk is None else self._heads(pk), None if pv is None else self._heads(pv),
+            window=window, scale=self.scale,
+            inv_freq=None if self.rope is None else self.rope.inv_freq,
+            dropout_p=self.dropout.p, training=self.training, use_kernels=self.use_kernels)
+        return F.linear(o.reshape(*q.shape[:-1], self.dim), self.proj_out.weight)
+
+
+class SlidingWindowAttention(_AttentionBase):
+    """Causal sliding-window attention with an always-visible prefix (MAG/MAL core)."""
+
+    def __init__(self, config: TitansConfig) -> None:
+        super().__init__(config)
+        self.window_size = config.window_size
+
+    def forward(self, x: torch.Tensor, prefix: torch.Tensor | None = None,
+                seq_offset: int = 0) -> torch.Tensor:
+        """``x`` [B, T, D], ``prefix`` [B, P, D] or None.
+
+        ``seq_offset`` shifts every RoPE position by the same amount; rotary
+        scores depend only on position differences, so the output does not
+        change with it (the argument is kept for API compatibility).
+        """
+        del seq_offset
+        w = torch.cat([self.proj_q.weight, self.proj_k.weight, self.proj_v.weight], dim=0)
+        qkv = F.linear(x, w)
+        D = self.dim
+        q, k, v = qkv[..., :D], qkv[..., D:2 * D], qkv[..., 2 * D:]
+        pk = pv = None
+        if prefix is not None and prefix.shape[1] > 0:
+            pkv = F.linear(prefix, w[D:])
+            pk, pv = pkv[..., :D], pkv[..., D:]
+        return self._attend(q, k, v, pk, pv, self.window_size)
+
+    # Mask helpers (same contract as the reference's, used by tests and debugging)
+    def _create_sliding_window_mask(self, seq_len: int, device) -> torch.Tensor:
+        return prefix_window_mask(seq_len, 0, self.window_size, device)
+
+    def _create_extended_mask(self, query_len: int, key_len: int, prefix_len: int, device) -> torch.Tensor:
+        assert key_len == prefix_len + query_len or key_len == prefix_len
+        if key_len == prefix_len:
+            m = torch.ones(query_len, prefix_len, dtype=torch.bool, device=device)
+        else:
+            m = prefix_window_mask(query_len, prefix_len, self.window_size, device)
+        return m[None, None]
+
+
+class SegmentedAttention(_AttentionBase):
+    """Causal attention over ``[persistent || memory || x]``; returns the ``x`` rows (MAC core)."""
+
+    def forward(self, x: torch.Tensor, persistent: torch.Tensor | None = None,
+                memory: torch.Tensor | None = None) -> torch.Tensor:
+        B = x.shape[0]
+        D = self.dim
+        w = torch.cat([self.proj_q.weight, self.proj_k.weight, self.proj_v.weight], dim=0)
+        qkv = F.linear(x, w)
+        q, k, v = qkv[..., :D], qkv[..., D:2 * D], qkv[..., 2 * D:]
+        parts = [p for p in (persistent, memory) if p is not None and p.shape[1] > 0]
+        pk = pv = None
+        if parts:
+            if len(parts) == 2 and persistent.stride(0) == 0:
+                # shared persistent rows: project once, then broadcast over the batch
+                pkv_p = F.linear(persistent[:1], w[D:]).expand(B, -1, -1)
+                pkv_m = F.linear(memory, w[D:])
+                pkv = torch.cat([pkv_p, pkv_m], dim=1)
+            else:
+                pkv = F.linear(torch.cat(parts, dim=1), w[D:])
+            pk, pv = pkv[..., :D], pkv[..., D:]
+        return self._attend(q, k, v, pk, pv, None)
+
+    def _create_causal_mask(self, seq_len: int, device) -> torch.Tensor:
+        return torch.tril(torch.ones(seq_len, seq_len, dtype=torch.bool, device=device))[None, None]

@@ -1,0 +1,209 @@
+"""Neural long-term memory (the Titans test-time-learning memory).
+
+Public surface follows the reference (`src/titans/memory.py:64-530`):
+``MemoryState`` (weights + momentum lists, ``detach``/``clone``),
+``MemoryMLP`` (``layers`` of bias-free Linears, ``get_weights``/``set_weights``/
+``compute_loss``) and ``NeuralLongTermMemory`` (``proj_k/v/q``, depthwise
+``conv_k/v/q``, ``memory``, ``gate_decay/lr/momentum``, ``proj_out``;
+``forward(x, state, return_state)``, ``retrieve``, ``init_state``).
+
+``semantics="ref"`` (default) reproduces the reference's CUDA behaviour,
+including that ``set_weights`` writes the state into the parameters' storage
+(`memory.py:162-165`), so a MAC forward leaves the last chunk's memory in the
+parameters and the backward reads those values.  ``semantics="paper"`` is the
+paper's per-sample, per-head memory with per-token gates and a chunked update
+(see :mod:`titans_pytorch_b200.ops.memory_paper`).
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from ..config import TitansConfig
+from ..ops.conv import conv_silu_norm
+from ..ops.memory import (activation_fn, memory_grads_reference, memory_step,
+                          mlp_forward_reference)
+
+
+def get_activation(name: str) -> nn.Module:
+    table = {"silu": nn.SiLU, "gelu": nn.GELU, "relu": nn.ReLU}
+    if name not in table:
+        raise ValueError(f"Unknown activation: {name}")
+    return table[name]()
+
+
+@dataclass
+class MemoryState:
+    """Memory weights and surprise momentum carried between calls/chunks."""
+
+    weights: list[torch.Tensor]
+    momentum: list[torch.Tensor]
+
+    def detach(self) -> "MemoryState":
+        return MemoryState([w.detach() for w in self.weights], [m.detach() for m in self.momentum])
+
+    def clone(self) -> "MemoryState":
+        return MemoryState([w.clone() for w in self.weights], [m.clone() for m in self.momentum])
+
+    def to(self, *args, **kwargs) -> "MemoryState":
+        return MemoryState([w.to(*args, **kwargs) for w in self.weights],
+                           [m.to(*args, **kwargs) for m in self.momentum])
+
+
+class MemoryMLP(nn.Module):
+    """The memory itself: L_M = 1 is one D x D matrix; L_M >= 2 is D -> H -> ... -> D."""
+
+    def __init__(self, config: TitansConfig) -> None:
+        super().__init__()
+        self.config = config
+        self.num_layers = config.num_memory_layers
+        self.dim = config.dim
+        self.hidden_dim = config.memory_hidden_dim
+        dims = ([self.dim, self.dim] if self.num_layers == 1 else
+                [self.dim] + [self.hidden_dim] * (self.num_layers - 1) + [self.dim])
+        self.layers = nn.ModuleList(nn.Linear(dims[i], dims[i + 1], bias=False)
+                                    for i in range(self.num_layers))
+        self.activation = get_activation(config.activation)
+        for layer in self.layers:
+            nn.init.normal_(layer.weight, std=config.init_std)
+
+    def weight_list(self) -> list[torch.Tensor]:
+        return [layer.weight for layer in self.layers]
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        return mlp_forward_reference(x, self.weight_list(), self.config.activation)
+
+    def get_weights(self) -> list[torch.Tensor]:
+        return [layer.weight.detach().clone() for layer in self.layers]
+
+    def set_weights(self, weights: list[torch.Tensor]) -> None:
+        """Write ``weights`` into the parameters' storage (not tracked by autograd)."""
+        with torch.no_grad():
+            for layer, w in zip(self.layers, weights, strict=True):
+                if layer.weight.data.data_ptr() != w.data_ptr():
+                    layer.weight.data.copy_(w)
+
+    def compute_loss(self, keys: torch.Tensor, values: torch.Tensor) -> torch.Tensor:
+        return F.mse_loss(self(keys), values, reduction="mean")
+
+
+class NeuralLongTermMemory(nn.Module):
+    def __init__(self, config: TitansConfig) -> None:
+        super().__init__()
+        self.config = config
+        self.dim = config.dim
+        D = config.dim
+        self.use_kernels = config.use_kernels
+        self.proj_k = nn.Linear(D, D, bias=False)
+        self.proj_v = nn.Linear(D, D, bias=False)
+        self.proj_q = nn.Linear(D, D, bias=False)
+        self.use_conv = config.use_conv
+        if self.use_conv:
+            ks = config.conv_kernel_size
+            self.conv_k = nn.Conv1d(D, D, ks, padding=ks - 1, groups=D)
+            self.conv_v = nn.Conv1d(D, D, ks, padding=ks - 1, groups=D)
+            self.conv_q = nn.Conv1d(D, D, ks, padding=ks - 1, groups=D)
+        self.memory = MemoryMLP(config)
+        self.gate_decay = nn.Sequential(nn.Linear(D, D), nn.Sigmoid())
+        self.gate_lr = nn.Sequential(nn.Linear(D, D), nn.Sigmoid())
+        self.gate_momentum = nn.Sequential(nn.Linear(D, D), nn.Sigmoid())
+        self.proj_out = nn.Linear(D, D, bias=False)
+        for m in (self.proj_k, self.proj_v, self.proj_q, self.proj_out):
+            nn.init.normal_(m.weight, std=config.init_std)
+
+    # ------------------------------------------------------------------ helpers
+    def _conv(self, name: str):
+        if not self.use_conv:
+            return None, None
+        c = getattr(self, name)
+        return c.weight, c.bias
+
+    def _gate_params(self):
+        g = (self.gate_decay[0], self.gate_lr[0], self.gate_momentum[0])
+        return [m.weight for m in g], [m.bias for m in g]
+
+    def _queries(self, x: torch.Tensor) -> torch.Tensor:
+        wq, bq = self._conv("conv_q")
+        return conv_silu_norm(F.linear(x, self.proj_q.weight), wq, bq, True, self.use_kernels)
+
+    @torch.no_grad()
+    def _keys_values(self, x: torch.Tensor):
+        D = self.dim
+        kv = F.linear(x, torch.cat([self.proj_k.weight, self.proj_v.weight], dim=0))
+        wk, bk = self._conv("conv_k")
+        wv, bv = self._conv("conv_v")
+        k = conv_silu_norm(kv[..., :D], wk, bk, True, self.use_kernels)
+        v = conv_silu_norm(kv[..., D:], wv, bv, False, self.use_kernels)
+        return k, v
+
+    def _apply_conv(self, k, v, q):
+        """Causal depthwise convolution of k, v, q (no activation); API parity helper."""
+        from ..ops.conv import causal_dwconv_reference
+        if not self.use_conv:
+            return k, v, q
+        return (causal_dwconv_reference(k, self.conv_k.weight, self.conv_k.bias),
+                causal_dwconv_reference(v, self.conv_v.weight, self.conv_v.bias),
+                causal_dwconv_reference(q, self.conv_q.weight, self.conv_q.bias))
+
+    @property
+    def _linear_silu(self) -> bool:
+        """L_M = 1 without conv takes the reference's analytic SiLU gradient."""
+        return self.config.num_memory_layers == 1 and not self.use_conv
+
+    @property
+    def _freezes_mlp(self) -> bool:
+        """L_M = 1 with conv: the reference's fallback path leaves the MLP frozen."""
+        return self.config.num_memory_layers == 1 and self.use_conv
+
+    def _compute_gradients(self, keys: torch.Tensor, values: torch.Tensor) -> list[torch.Tensor]:
+        """Associative-loss gradient at the current memory weights (ref semantics)."""
+        with torch.no_grad():
+            g = memory_grads_reference(keys.detach(), values.detach(),
+                                       [w.detach() for w in self.memory.weight_list()],
+                                       self.config.activation, self._linear_silu)
+        if self._freezes_mlp:
+            self.memory.requires_grad_(False)
+        return g
+
+    # --------------------------------------------------------------------- API
+    def init_state(self, _batch_size: int = 1, _device=None) -> MemoryState:
+        w = self.memory.get_weights()
+        return MemoryState(weights=w, momentum=[torch.zeros_like(t) for t in w])
+
+    def _update(self, x: torch.Tensor, state: MemoryState) -> MemoryState:
+        """New state after one update with the tokens of ``x`` (no retrieval output)."""
+        k, v = self._keys_values(x)
+        gw, gb = self._gate_params()
+        new_w, new_m = memory_step(k, v, x.detach(), state.weights, state.momentum, gw, gb,
+                                   self.config.memory_lr, self.config.memory_momentum,
+                                   self.config.activation, self._linear_silu, self.use_kernels)
+        if self._freezes_mlp:
+            self.memory.requires_grad_(False)
+        return MemoryState(new_w, new_m).detach()
+
+    def forward(self, x: torch.Tensor, state: MemoryState | None = None,
+                return_state: bool = True):
+        """Retrieve with the incoming memory and update it with ``x``.
+
+        Returns ``(proj_out(M_{t-1}(q)), new_state or None)``.
+        """
+        if state is None:
+            state = self.init_state(x.shape[0], x.device)
+        else:
+            self.memory.set_weights(state.weights)
+        retrieved = self.memory(self._queries(x))
+        new_state = self._update(x, state)
+        out = F.linear(retrieved, self.proj_out.weight)
+        return (out, new_state) if return_state else (out, None)
+
+    def retrieve(self, queries: torch.Tensor, state: MemoryState) -> torch.Tensor:
+        """proj_out(M(q)) with the memory set to ``state`` (no update)."""
+        self.memory.set_weights(state.weights)
+        return F.linear(self.memory(self._queries(queries)), self.proj_out.weight)
+
+
+__all__ = ["MemoryState", "MemoryMLP", "NeuralLongTermMemory", "get_activation", "activation_fn"]

@@ -1,0 +1,196 @@
+"""Titans model variants: MAC (memory as context), MAG (as gate), MAL (as layer), LMM.
+
+Block structure, parameter names and ``forward(input_ids, states=None) ->
+(logits, states)`` follow the reference (`src/titans/models.py:144-737`):
+
+* MAC (`:144-323`): per ``chunk_size`` segment, every block retrieves from its
+  memory, attends over ``[persistent || norm(retrieved) || x]``, updates its
+  memory with the attention output ``y`` and gates ``y * retrieve(y)``; chunks
+  are the outer loop, blocks the inner loop.
+* MAG (`:331-473`): ``y = x + SWA(norm1 x)``; ``o = y * Mem(norm1 x)``; FFN.
+* MAL (`:481-615`): ``x += Mem(norm1 x)``; ``x += SWA(norm2 x)``; FFN.
+* LMM (`:623-737`): ``x += Mem(norm1 x)``; FFN.
+
+All four tie ``head.weight`` to ``embed.weight`` and initialise the embedding
+with N(0, init_std).  Submodule registration order matches the reference so
+``state_dict`` keys come out in the same order.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from ..config import TitansConfig
+from .attention import SegmentedAttention, SlidingWindowAttention
+from .layers import FeedForward, RMSNorm
+from .memory import MemoryState, NeuralLongTermMemory
+from .persistent import PersistentMemory
+
+
+def _norm(config: TitansConfig) -> RMSNorm:
+    return RMSNorm(config.dim, config.norm_eps, config.use_kernels)
+
+
+class MACBlock(nn.Module):
+    def __init__(self, config: TitansConfig) -> None:
+        super().__init__()
+        self.config = config
+        self.memory = NeuralLongTermMemory(config)
+        self.persistent = PersistentMemory(config)
+        self.attention = SegmentedAttention(config)
+        self.ffn = FeedForward(config)
+        self.norm1 = _norm(config)
+        self.norm2 = _norm(config)
+        self.norm_mem = _norm(config)
+        self.dropout = nn.Dropout(config.dropout)
+
+    def forward(self, x: torch.Tensor, state: MemoryState | None = None):
+        B = x.shape[0]
+        if state is None:
+            state = self.memory.init_state(B, x.device)
+        h = self.norm_mem(self.memory.retrieve(x, state))
+        attn = self.attention(self.norm1(x), persistent=self.persistent(B), memory=h)
+        y = x + self.dropout(attn)
+        # The reference calls memory(y, state) here and discards its retrieval
+        # output; only the updated state is used, so only the update runs.
+        new_state = self.memory._update(y, state)
+        out = y * self.memory.retrieve(y, new_state)
+        out = out + self.dropout(self.ffn(self.norm2(out)))
+        return out, new_state
+
+
+class MAGBlock(nn.Module):
+    def __init__(self, config: TitansConfig) -> None:
+        super().__init__()
+        self.config = config
+        self.persistent = PersistentMemory(config)
+        self.attention = SlidingWindowAttention(config)
+        self.memory = NeuralLongTermMemory(config)
+        self.ffn = FeedForward(config)
+        self.norm1 = _norm(config)
+        self.norm2 = _norm(config)
+        self.dropout = nn.Dropout(config.dropout)
+
+    def forward(self, x: torch.Tensor, state: MemoryState | None = None):
+        n = self.norm1(x)
+        y = x + self.dropout(self.attention(n, prefix=self.persistent(x.shape[0])))
+        m, new_state = self.memory(n, state=state)
+        out = y * m
+        out = out + self.dropout(self.ffn(self.norm2(out)))
+        return out, new_state
+
+
+class MALBlock(nn.Module):
+    def __init__(self, config: TitansConfig) -> None:
+        super().__init__()
+        self.config = config
+        self.persistent = PersistentMemory(config)
+        self.memory = NeuralLongTermMemory(config)
+        self.attention = SlidingWindowAttention(config)
+        self.ffn = FeedForward(config)
+        self.norm1 = _norm(config)
+        self.norm2 = _norm(config)
+        self.norm3 = _norm(config)
+        self.dropout = nn.Dropout(config.dropout)
+
+    def forward(self, x: torch.Tensor, state: MemoryState | None = None):
+        m, new_state = self.memory(self.norm1(x), state=state)
+        x = x + self.dropout(m)
+        x = x + self.dropout(self.attention(self.norm2(x), prefix=self.persistent(x.shape[0])))
+        x = x + self.dropout(self.ffn(self.norm3(x)))
+        return x, new_state
+
+
+class LMMBlock(nn.Module):
+    def __init__(self, config: TitansConfig) -> None:
+        super().__init__()
+        self.config = config
+        self.memory = NeuralLongTermMemory(config)
+        self.ffn = FeedForward(config)
+        self.norm1 = _norm(config)
+        self.norm2 = _norm(config)
+        self.dropout = nn.Dropout(config.dropout)
+
+    def forward(self, x: torch.Tensor, state: MemoryState | None = None):
+        m, new_state = self.memory(self.norm1(x), state=state)
+        x = x + self.dropout(m)
+        x = x + self.dropout(self.ffn(self.norm2(x)))
+        return x, new_state
+
+
+class _TitansLM(nn.Module):
+    """Embedding -> blocks -> RMSNorm -> tied head."""
+
+    block_cls: type[nn.Module]
+    model_type: str
+
+    def __init__(self, config: TitansConfig) -> None:
+        super().__init__()
+        self.config = config
+        self.embed = nn.Embedding(config.vocab_size, config.dim)
+        self.blocks = nn.ModuleList(self.block_cls(config) for _ in range(config.num_layers))
+        self.norm = _norm(config)
+        self.head = nn.Linear(config.dim, config.vocab_size, bias=False)
+        self.head.weight = self.embed.weight
+        nn.init.normal_(self.embed.weight, std=config.init_std)
+
+    def _run_blocks(self, x, states):
+        new_states = []
+        for block, st in zip(self.blocks, states, strict=True):
+            x, ns = block(x, state=st)
+            new_states.append(ns)
+        return x, new_states
+
+    def hidden_states(self, input_ids: torch.Tensor, states=None):
+        """Final-norm hidden states [B, T, D] and new memory states (no head GEMM)."""
+        if states is None:
+            states = [None] * len(self.blocks)
+        x, new_states = self._run_blocks(self.embed(input_ids), states)
+        return self.norm(x), new_states
+
+    def forward(self, input_ids: torch.Tensor, states: list[MemoryState] | None = None):
+        h, new_states = self.hidden_states(input_ids, states)
+        return F.linear(h, self.head.weight), new_states
+
+
+class TitansMAC(_TitansLM):
+    block_cls = MACBlock
+    model_type = "mac"
+
+    def hidden_states(self, input_ids: torch.Tensor, states=None):
+        if states is None:
+            states = [None] * len(self.blocks)
+        x = self.embed(input_ids)
+        cs = self.config.chunk_size
+        outs = []
+        for s in range(0, x.shape[1], cs):
+            chunk, states = self._run_blocks(x[:, s:s + cs], states)
+            outs.append(chunk)
+        return self.norm(torch.cat(outs, dim=1)), states
+
+
+class TitansMAG(_TitansLM):
+    block_cls = MAGBlock
+    model_type = "mag"
+
+
+class TitansMAL(_TitansLM):
+    block_cls = MALBlock
+    model_type = "mal"
+
+
+class TitansLMM(_TitansLM):
+    block_cls = LMMBlock
+    model_type = "lmm"
+
+
+MODEL_CLASSES = {"mac": TitansMAC, "mag": TitansMAG, "mal": TitansMAL, "lmm": TitansLMM}
+
+
+def create_model(model_type: str, config: TitansConfig) -> _TitansLM:
+    try:
+        return MODEL_CLASSES[model_type.lower()](config)
+    except KeyError:
+        raise ValueError(f"Unknown model type: {model_type}") from None

@@ -1,0 +1,129 @@
+"""Windowed causal attention with always-visible prefix keys and fused RoPE.
+
+One op serves both attention forms of the reference:
+
+* sliding-window attention (`src/titans/attention.py:135-307`): queries come
+  from ``x`` only, keys/values from ``[prefix || x]``; a query at main
+  position i sees every prefix key and main keys j with ``j <= i`` and
+  ``i - j < window``.  RoPE positions are ``P + i`` for queries, ``p`` for
+  prefix keys and ``P + j`` for main keys (`attention.py:248-251`).
+* MAC segmented attention (`attention.py:355-424`): causal attention over
+  ``[persistent || memory || x]`` whose output is kept only for the ``x``
+  rows.  Those rows see the whole prefix and causal main keys, i.e. the same
+  rule with an infinite window, so the discarded prefix query rows are never
+  computed.
+
+RoPE is the interleaved-pair rotation of the reference (`attention.py:107-132`),
+base 10000, applied on load inside the CUDA kernel (``csrc/attention.cu``).
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.nn.functional as F
+
+from ._ext import ext, want_kernels
+
+NO_WINDOW = 1 << 30
+
+
+def rope_angles(positions: torch.Tensor, inv_freq: torch.Tensor):
+    freqs = torch.outer(positions.float(), inv_freq.float())
+    return freqs.cos(), freqs.sin()
+
+
+def apply_rope_reference(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+    """Rotate interleaved pairs (x[..., 2i], x[..., 2i+1]) of ``x`` [B, S, H, d]."""
+    cos = cos.to(x.dtype)[None, :, None, :]
+    sin = sin.to(x.dtype)[None, :, None, :]
+    x1, x2 = x[..., 0::2], x[..., 1::2]
+    out = torch.empty_like(x)
+    out[..., 0::2] = x1 * cos - x2 * sin
+    out[..., 1::2] = x1 * sin + x2 * cos
+    return out
+
+
+def prefix_window_mask(q_len: int, prefix_len: int, window: int, device) -> torch.Tensor:
+    """Boolean [q_len, prefix_len + q_len] mask (True = attend)."""
+    i = torch.arange(q_len, device=device)[:, None]
+    j = torch.arange(q_len, device=device)[None, :]
+    main = (j <= i) & ((i - j) < window)
+    pre = torch.ones(q_len, prefix_len, dtype=torch.bool, device=device)
+    return torch.cat([pre, main], dim=1)
+
+
+def window_attention_reference(q, k, v, pk, pv, window, scale, inv_freq, dropout_p=0.0, training=False):
+    """PyTorch restatement (dense mask + SDPA); tensors are [B, S, H, d]."""
+    B, T, H, d = q.shape
+    P = 0 if pk is None else pk.shape[1]
+    if P:
+        pk = pk.expand(B, -1, -1, -1)
+        pv = pv.expand(B, -1, -1, -1)
+        kf = torch.cat([pk, k], dim=1)
+        vf = torch.cat([pv, v], dim=1)
+    else:
+        kf, vf = k, v
+    if inv_freq is not None:
+        cq, sq = rope_angles(torch.arange(P, P + T, device=q.device), inv_freq)
+        ck, sk = rope_angles(torch.arange(0, P + T, device=q.device), inv_freq)
+        q = apply_rope_reference(q, cq, sq)
+        kf = apply_rope_reference(kf, ck, sk)
+    mask = prefix_window_mask(T, P, window, q.device)
+    add = torch.zeros(mask.shape, dtype=q.dtype, device=q.device).masked_fill_(~mask, float("-inf"))
+    o = F.scaled_dot_product_attention(
+        q.transpose(1, 2), kf.transpose(1, 2), vf.transpose(1, 2), attn_mask=add,
+        dropout_p=dropout_p if training else 0.0, is_causal=False, scale=scale)
+    return o.transpose(1, 2)
+
+
+class _WindowAttnFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, k, v, pk, pv, window, scale, inv_freq):
+        o, lse = ext().attn_fwd(q, k, v, pk, pv, int(window), float(scale), inv_freq)
+        ctx.save_for_backward(q, k, v, pk, pv, inv_freq, o, lse)
+        ctx.window, ctx.scale = int(window), float(scale)
+        ctx.has_prefix = pk is not None
+        return o
+
+    @staticmethod
+    def backward(ctx, do):
+        q, k, v, pk, pv, inv_freq, o, lse = ctx.saved_tensors
+        dq, dk, dv, dpk, dpv = ext().attn_bwd(do.contiguous(), q, k, v, pk, pv, o, lse,
+                                              ctx.window, ctx.scale, inv_freq)
+        if not ctx.has_prefix:
+            dpk = dpv = None
+        return dq, dk, dv, dpk, dpv, None, None, None
+
+
+def window_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                     pk: torch.Tensor | None = None, pv: torch.Tensor | None = None,
+                     window: int | None = None, scale: float | None = None,
+                     inv_freq: torch.Tensor | None = None, dropout_p: float = 0.0,
+                     training: bool = False, use_kernels: bool | None = None) -> torch.Tensor:
+    """Attention of ``q`` over ``[pk || k]`` with the prefix/window rule above.
+
+    Shapes: ``q, k, v`` are ``[B, T, H, d]`` (the head dim must be contiguous;
+    rows may be strided, e.g. slices of a fused QKV projection); ``pk, pv`` are
+    ``[B or 1, P, H, d]`` or ``None``.  ``window=None`` means no window (MAC).
+    Returns ``[B, T, H, d]`` contiguous.
+    """
+    window = NO_WINDOW if window is None else int(window)
+    scale = (q.shape[-1] ** -0.5) if scale is None else scale
+    if want_kernels(q, use_kernels):
+        if dropout_p > 0.0 and training:
+            raise NotImplementedError("attention-probability dropout is not implemented in the "
+                                      "sm_100a attention kernel; set dropout=0")
+        return _WindowAttnFn.apply(q, k, v, pk, pv, window, scale, inv_freq)
+    return window_attention_reference(q, k, v, pk, pv, window, scale, inv_freq, dropout_p, training)
+
+
+def attention_flops(B: int, T: int, H: int, d: int, P: int, window: int | None) -> float:
+    """Forward FLOPs actually needed (visible keys only): 4 * d per (query, key) pair."""
+    w = T if window is None else min(window, T)
+    # main keys: sum_i min(i+1, w)
+    main = w * (w + 1) / 2 + max(T - w, 0) * w
+    return 4.0 * d * H * B * (main + P * T)
+
+
+__all__ = ["window_attention", "window_attention_reference", "apply_rope_reference",
+           "rope_angles", "prefix_window_mask", "attention_flops", "NO_WINDOW"]

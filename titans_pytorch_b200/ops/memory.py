@@ -1,0 +1,133 @@
+"""Neural-memory math: retrieval MLP, associative-loss gradient, gated update.
+
+Reference semantics (``semantics="ref"``), as run by the reference on CUDA:
+
+* gradient of ``mean_{B,T,D} (MLP_W(k) - v)^2`` w.r.t. every memory weight,
+  with k and v detached (`src/titans/memory.py:287-351`; CUDA branch
+  `src/titans/cuda_optimizations.py:228-319`).
+* one-layer memory (L_M = 1): the reference's CUDA branch has its own analytic
+  form ``2/(B*T) * (silu(k) W^T - v)^T silu(k)`` (`cuda_optimizations.py:248-275`),
+  but it calls ``.view`` on the keys, which are non-contiguous whenever the
+  depthwise conv is on (`memory.py:263-285` transposes around the conv); the
+  resulting exception sends it to the autograd fallback (`memory.py:319-346`),
+  i.e. the plain mse gradient, which also switches ``requires_grad`` off on
+  the memory MLP.  ``linear_silu=True`` selects the analytic form (L_M = 1,
+  no conv); otherwise the plain gradient is used.
+* scalar gates alpha/theta/eta: the mean over batch and channels of
+  ``sigmoid(Linear(mean_T x))`` (`memory.py:427-432`).
+* ``S' = eta*S - theta*G``,  ``W' = (1-alpha)*W + S'`` (`memory.py:464-498`).
+
+The deep-memory gradient is written out as explicit back-propagation through
+the MLP (no inner autograd graph), which is the same arithmetic the CUDA path
+runs as tcgen05/cuBLAS GEMMs with fused activation epilogues
+(``csrc/memory.cu``): every step stays on the device and the gates never
+leave it (no ``.item()`` host sync).
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.nn.functional as F
+
+from ._ext import ext, want_kernels
+
+
+def activation_fn(name: str):
+    if name == "silu":
+        return F.silu
+    if name == "gelu":
+        return F.gelu
+    if name == "relu":
+        return F.relu
+    raise ValueError(f"Unknown activation: {name}")
+
+
+def activation_grad(name: str, z: torch.Tensor) -> torch.Tensor:
+    """d act(z) / dz, elementwise."""
+    if name == "silu":
+        s = torch.sigmoid(z)
+        return s * (1 + z * (1 - s))
+    if name == "gelu":  # exact (erf) GELU, nn.GELU's default
+        return 0.5 * (1 + torch.erf(z / math.sqrt(2.0))) + z * torch.exp(-0.5 * z * z) / math.sqrt(2 * math.pi)
+    if name == "relu":
+        return (z > 0).to(z.dtype)
+    raise ValueError(f"Unknown activation: {name}")
+
+
+def mlp_forward_reference(x: torch.Tensor, weights: list[torch.Tensor], act: str) -> torch.Tensor:
+    h = x
+    f = activation_fn(act)
+    for i, w in enumerate(weights):
+        h = F.linear(h, w)
+        if i < len(weights) - 1:
+            h = f(h)
+    return h
+
+
+def memory_grads_reference(k: torch.Tensor, v: torch.Tensor, weights: list[torch.Tensor],
+                           act: str, linear_silu: bool = False) -> list[torch.Tensor]:
+    """Gradient of the associative-memory loss for every memory weight (ref semantics)."""
+    B, T, D = k.shape
+    f = activation_fn(act)
+    k2 = k.reshape(-1, D)
+    v2 = v.reshape(-1, v.shape[-1])
+    if len(weights) == 1 and linear_silu:
+        h = f(k2)
+        diff = F.linear(h, weights[0]) - v2
+        return [(diff.t() @ h) * (2.0 / (B * T))]
+    hs = [k2]
+    zs = []
+    h = k2
+    for i, w in enumerate(weights):
+        z = F.linear(h, w)
+        if i < len(weights) - 1:
+            zs.append(z)
+            h = f(z)
+            hs.append(h)
+        else:
+            h = z
+    delta = (h - v2) * (2.0 / h.numel())
+    grads = [None] * len(weights)
+    for i in range(len(weights) - 1, -1, -1):
+        grads[i] = delta.t() @ hs[i]
+        if i > 0:
+            delta = (delta @ weights[i]) * activation_grad(act, zs[i - 1])
+    return grads
+
+
+def memory_gates_reference(x_mean: torch.Tensor, gate_ws, gate_bs, lr: float, mom: float):
+    """(alpha, theta, eta) as 0-dim tensors from ``x_mean`` [B, 1, D]."""
+    a = torch.sigmoid(F.linear(x_mean, gate_ws[0], gate_bs[0])).mean()
+    t = torch.sigmoid(F.linear(x_mean, gate_ws[1], gate_bs[1])).mean() * lr
+    e = torch.sigmoid(F.linear(x_mean, gate_ws[2], gate_bs[2])).mean() * mom
+    return a, t, e
+
+
+def memory_update_reference(weights, momentum, grads, alpha, eta, theta):
+    new_m = [eta * m - theta * g for m, g in zip(momentum, grads, strict=True)]
+    new_w = [(1 - alpha) * w + s for w, s in zip(weights, new_m, strict=True)]
+    return new_w, new_m
+
+
+@torch.no_grad()
+def memory_step(k: torch.Tensor, v: torch.Tensor, x_for_gates: torch.Tensor,
+                weights: list[torch.Tensor], momentum: list[torch.Tensor],
+                gate_ws, gate_bs, lr: float, mom: float, act: str,
+                linear_silu: bool = False, use_kernels: bool | None = None):
+    """One reference-semantics memory update; returns (new_weights, new_momentum).
+
+    ``k`` and ``v`` are the (already conv/SiLU/L2-processed) keys and values,
+    ``x_for_gates`` the memory input whose sequence mean drives the gates.
+    Nothing here is differentiated (the reference detaches k, v and the new
+    state, `memory.py:330-331, 461`).
+    """
+    if want_kernels(k, use_kernels):
+        return ext().memory_step(k, v, x_for_gates, list(weights), list(momentum),
+                                 list(gate_ws), list(gate_bs), float(lr), float(mom), act,
+                                 bool(linear_silu))
+    x_mean = x_for_gates.float().mean(dim=1, keepdim=True).to(x_for_gates.dtype)
+    alpha, theta, eta = memory_gates_reference(x_mean, gate_ws, gate_bs, lr, mom)
+    grads = memory_grads_reference(k, v, weights, act, linear_silu)
+    return memory_update_reference(weights, momentum, grads, alpha, eta, theta)

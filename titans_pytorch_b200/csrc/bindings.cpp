@@ -1,0 +1,71 @@
+// Python bindings of the sm_100a kernel library (module titans_pytorch_b200._C).
+#include <torch/extension.h>
+
+#include <vector>
+
+namespace tb {
+// norm.cu
+std::vector<at::Tensor> rms_norm_fwd(const at::Tensor& x, const at::Tensor& w, double eps);
+std::vector<at::Tensor> rms_norm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& w,
+                                     const at::Tensor& rstd, bool need_dw);
+// conv.cu
+at::Tensor conv_silu_norm_fwd(const at::Tensor& x, const c10::optional<at::Tensor>& w,
+                              const c10::optional<at::Tensor>& b, bool normalize);
+std::vector<at::Tensor> conv_silu_norm_bwd(const at::Tensor& dy, const at::Tensor& x,
+                                           const c10::optional<at::Tensor>& w, const c10::optional<at::Tensor>& b,
+                                           bool normalize, bool need_wgrad);
+// elementwise.cu
+at::Tensor swiglu_fwd(const at::Tensor& gu);
+at::Tensor swiglu_bwd(const at::Tensor& dh, const at::Tensor& gu);
+at::Tensor memory_gates(const at::Tensor& x, const std::vector<at::Tensor>& ws, const std::vector<at::Tensor>& bs,
+                        double lr, double mom);
+void act_inplace(const at::Tensor& z, at::Tensor& a, const std::string& act);
+void act_grad_mul(at::Tensor& gr, const at::Tensor& z, const std::string& act);
+void scaled_err(at::Tensor& p, const at::Tensor& v, double scale);
+std::vector<at::Tensor> mem_update(const at::Tensor& w, const at::Tensor& m, const at::Tensor& grad,
+                                   const at::Tensor& gates);
+// loss.cu
+std::vector<at::Tensor> cross_entropy_fwd(const at::Tensor& logits, const at::Tensor& labels, int64_t ignore_index);
+at::Tensor cross_entropy_bwd(const at::Tensor& logits, const at::Tensor& labels, const at::Tensor& lse,
+                             const at::Tensor& stats, const at::Tensor& gout, int64_t ignore_index);
+// optim.cu
+at::Tensor grad_norm_clip(const at::Tensor& grads, const at::Tensor& tab, int64_t nseg, int64_t items, double gscale,
+                          double max_norm);
+void adamw_step(at::Tensor& master, at::Tensor& exp_avg, at::Tensor& exp_avg_sq, const at::Tensor& grads,
+                const c10::optional<at::Tensor>& params_out, const at::Tensor& tab, int64_t nseg, int64_t items,
+                const c10::optional<at::Tensor>& clip, double gscale, double lr, double beta1, double beta2,
+                double eps, double wd, int64_t step);
+// attention.cu
+std::vector<at::Tensor> attn_pack(const at::Tensor& qkv, const c10::optional<at::Tensor>& pkv, int64_t H,
+                                  const c10::optional<at::Tensor>& inv_freq);
+std::vector<at::Tensor> attn_fwd_packed(const at::Tensor& Q, const at::Tensor& K, const at::Tensor& V, int64_t window,
+                                        double scale);
+std::vector<at::Tensor> attn_bwd_packed(const at::Tensor& dO, const at::Tensor& Q, const at::Tensor& K,
+                                        const at::Tensor& V, const at::Tensor& O, const at::Tensor& LSE,
+                                        int64_t window, double scale);
+std::vector<at::Tensor> attn_unpack(const at::Tensor& dQa, const at::Tensor& dKa, const at::Tensor& dVa,
+                                    const c10::optional<at::Tensor>& inv_freq, int64_t Bp, at::ScalarType dtype);
+}  // namespace tb
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "titans_pytorch_b200 sm_100a kernels";
+  m.def("rms_norm_fwd", &tb::rms_norm_fwd);
+  m.def("rms_norm_bwd", &tb::rms_norm_bwd);
+  m.def("conv_silu_norm_fwd", &tb::conv_silu_norm_fwd);
+  m.def("conv_silu_norm_bwd", &tb::conv_silu_norm_bwd);
+  m.def("swiglu_fwd", &tb::swiglu_fwd);
+  m.def("swiglu_bwd", &tb::swiglu_bwd);
+  m.def("memory_gates", &tb::memory_gates);
+  m.def("act_inplace", &tb::act_inplace);
+  m.def("act_grad_mul", &tb::act_grad_mul);
+  m.def("scaled_err", &tb::scaled_err);
+  m.def("mem_update", &tb::mem_update);
+  m.def("cross_entropy_fwd", &tb::cross_entropy_fwd);
+  m.def("cross_entropy_bwd", &tb::cross_entropy_bwd);
+  m.def("grad_norm_clip", &tb::grad_norm_clip);
+  m.def("adamw_step", &tb::adamw_step);
+  m.def("attn_pack", &tb::attn_pack);
+  m.def("attn_fwd_packed", &tb::attn_fwd_packed);
+  m.def("attn_bwd_packed", &tb::attn_bwd_packed);
+  m.def("attn_unpack", &tb::attn_unpack);
+}

@@ -1,0 +1,151 @@
+// AdamW over flat parameter buffers, with the global-norm gradient clip
+// applied inside the update (the clip coefficient is computed on the device;
+// nothing is read back to the host).
+//
+// Buffers: master (fp32), exp_avg / exp_avg_sq (fp32), grads (bf16 or fp32),
+// optional low-precision parameter copy written from the updated master.
+// `segs` is a device int64 [nseg, 2] table of (offset, length) ranges that
+// received a gradient this step; parameters outside it are left untouched,
+// matching torch.optim.AdamW's skip of parameters whose .grad is None.
+#include "common.cuh"
+
+namespace tb {
+
+constexpr int kChunk = 1 << 14;  // elements per work item
+
+// work items: (segment, chunk within segment) enumerated by a prefix table
+// on the device: item_start[s] = first item of segment s.
+__device__ __forceinline__ int find_seg(const int64_t* __restrict__ item_start, int nseg, int64_t item) {
+  int lo = 0, hi = nseg - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (item_start[mid] <= item) lo = mid; else hi = mid - 1;
+  }
+  return lo;
+}
+
+template <typename G>
+__global__ void sumsq_kernel(const G* __restrict__ g, const int64_t* __restrict__ segs,
+                             const int64_t* __restrict__ item_start, int nseg, int64_t nitems, float scale,
+                             float* __restrict__ part) {
+  __shared__ float red[32];
+  float acc = 0.f;
+  for (int64_t it = blockIdx.x; it < nitems; it += gridDim.x) {
+    const int s = find_seg(item_start, nseg, it);
+    const int64_t off = segs[2 * s], len = segs[2 * s + 1];
+    const int64_t c0 = (it - item_start[s]) * kChunk;
+    const int64_t c1 = min(len, c0 + kChunk);
+    for (int64_t i = c0 + threadIdx.x; i < c1; i += blockDim.x) {
+      const float v = to_f<G>(g[off + i]) * scale;
+      acc += v * v;
+    }
+  }
+  acc = block_sum(acc, red);
+  if (threadIdx.x == 0) part[blockIdx.x] = acc;
+}
+
+// out[0] = total norm, out[1] = clip coefficient (1 when max_norm <= 0)
+__global__ void clip_coef_kernel(const float* __restrict__ part, int n, float max_norm, float* __restrict__ out) {
+  __shared__ float red[32];
+  float s = 0.f;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) s += part[i];
+  s = block_sum(s, red);
+  if (threadIdx.x == 0) {
+    const float nrm = sqrtf(s);
+    out[0] = nrm;
+    out[1] = max_norm > 0.f ? fminf(1.f, max_norm / (nrm + 1e-6f)) : 1.f;
+  }
+}
+
+template <typename G, typename P>
+__global__ void adamw_kernel(float* __restrict__ master, float* __restrict__ m, float* __restrict__ v,
+                             const G* __restrict__ g, P* __restrict__ pout, const int64_t* __restrict__ segs,
+                             const int64_t* __restrict__ item_start, int nseg, int64_t nitems,
+                             const float* __restrict__ clip, float gscale, float lr, float b1, float b2, float eps,
+                             float wd, float bc1, float bc2_sqrt) {
+  const float cg = gscale * (clip ? clip[1] : 1.f);
+  const float step = lr / bc1;
+  const float decay = 1.f - lr * wd;
+  for (int64_t it = blockIdx.x; it < nitems; it += gridDim.x) {
+    const int s = find_seg(item_start, nseg, it);
+    const int64_t off = segs[2 * s], len = segs[2 * s + 1];
+    const int64_t c0 = (it - item_start[s]) * kChunk;
+    const int64_t c1 = min(len, c0 + kChunk);
+    for (int64_t i = off + c0 + threadIdx.x; i < off + c1; i += blockDim.x) {
+      const float gr = to_f<G>(g[i]) * cg;
+      float p = master[i] * decay;
+      const float mi = b1 * m[i] + (1.f - b1) * gr;
+      const float vi = b2 * v[i] + (1.f - b2) * gr * gr;
+      m[i] = mi;
+      v[i] = vi;
+      p -= step * mi / (sqrtf(vi) / bc2_sqrt + eps);
+      master[i] = p;
+      if (pout) pout[i] = from_f<P>(p);
+    }
+  }
+}
+
+// `tab` (device int64): [off0, len0, off1, len1, ..., item_start0, item_start1, ...]
+// with item_start[s] = first kChunk-sized work item of segment s; built once
+// on the host by the Python optimizer and cached on the device.
+// Returns float[2] on device: (grad norm, clip coef).  `gscale` multiplies
+// the raw grads first (e.g. 1/world_size for averaged data-parallel grads).
+at::Tensor grad_norm_clip(const at::Tensor& grads, const at::Tensor& tab, int64_t nseg, int64_t items, double gscale,
+                          double max_norm) {
+  const at::cuda::CUDAGuard guard(grads.device());
+  at::Tensor out = at::zeros({2}, grads.options().dtype(at::kFloat));
+  if (nseg == 0) return out;
+  TORCH_CHECK(tab.is_cuda() && tab.scalar_type() == at::kLong && tab.numel() == 3 * nseg, "grad_norm: bad table");
+  const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>(items, num_sms() * 4));
+  at::Tensor part = at::empty({blocks}, grads.options().dtype(at::kFloat));
+  const int64_t* segs = tab.data_ptr<int64_t>();
+  const int64_t* istart = segs + 2 * nseg;
+  if (grads.scalar_type() == at::kBFloat16) {
+    sumsq_kernel<__nv_bfloat16><<<blocks, 512, 0, stream()>>>((const __nv_bfloat16*)grads.data_ptr(), segs, istart,
+                                                             nseg, items, (float)gscale, part.data_ptr<float>());
+  } else {
+    TORCH_CHECK(grads.scalar_type() == at::kFloat, "grad_norm: bf16 or fp32 grads");
+    sumsq_kernel<float><<<blocks, 512, 0, stream()>>>(grads.data_ptr<float>(), segs, istart, nseg, items,
+                                                      (float)gscale, part.data_ptr<float>());
+  }
+  clip_coef_kernel<<<1, 1024, 0, stream()>>>(part.data_ptr<float>(), blocks, (float)max_norm, out.data_ptr<float>());
+  check_launch("grad_norm_clip");
+  return out;
+}
+
+void adamw_step(at::Tensor& master, at::Tensor& exp_avg, at::Tensor& exp_avg_sq, const at::Tensor& grads,
+                const c10::optional<at::Tensor>& params_out, const at::Tensor& tab, int64_t nseg, int64_t items,
+                const c10::optional<at::Tensor>& clip, double gscale, double lr, double beta1, double beta2,
+                double eps, double wd, int64_t step) {
+  const at::cuda::CUDAGuard guard(master.device());
+  TORCH_CHECK(master.scalar_type() == at::kFloat && exp_avg.scalar_type() == at::kFloat &&
+                  exp_avg_sq.scalar_type() == at::kFloat, "adamw: fp32 master/state");
+  TORCH_CHECK(master.numel() == grads.numel() && master.is_contiguous() && grads.is_contiguous(), "adamw: sizes");
+  if (nseg == 0) return;
+  TORCH_CHECK(tab.is_cuda() && tab.scalar_type() == at::kLong && tab.numel() == 3 * nseg, "adamw: bad table");
+  const int64_t* segs = tab.data_ptr<int64_t>();
+  const int64_t* istart = segs + 2 * nseg;
+  const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>(items, num_sms() * 8));
+  const float bc1 = 1.f - (float)std::pow(beta1, (double)step);
+  const float bc2s = std::sqrt(1.f - (float)std::pow(beta2, (double)step));
+  const float* cl = (clip.has_value() && clip->defined()) ? clip->data_ptr<float>() : nullptr;
+  const bool has_out = params_out.has_value() && params_out->defined();
+  auto launch = [&](auto gtag, auto ptag) {
+    using G = decltype(gtag);
+    using P = decltype(ptag);
+    adamw_kernel<G, P><<<blocks, 512, 0, stream()>>>(
+        master.data_ptr<float>(), exp_avg.data_ptr<float>(), exp_avg_sq.data_ptr<float>(), (const G*)grads.data_ptr(),
+        has_out ? (P*)params_out->data_ptr() : nullptr, segs, istart, nseg, items, cl, (float)gscale, (float)lr,
+        (float)beta1, (float)beta2, (float)eps, (float)wd, bc1, bc2s);
+  };
+  const bool gb = grads.scalar_type() == at::kBFloat16;
+  const bool pb = !has_out || params_out->scalar_type() == at::kBFloat16;
+  if (has_out) TORCH_CHECK(params_out->numel() == master.numel(), "adamw: params_out size");
+  if (gb && pb) launch(__nv_bfloat16{}, __nv_bfloat16{});
+  else if (gb && !pb) launch(__nv_bfloat16{}, float{});
+  else if (!gb && pb) launch(float{}, __nv_bfloat16{});
+  else launch(float{}, float{});
+  check_launch("adamw_step");
+}
+
+}  // namespace tb

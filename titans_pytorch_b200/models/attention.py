@@ -78,18 +78,16 @@ class _AttentionBase(nn.Module):
         for m in (self.proj_q, self.proj_k, self.proj_v, self.proj_out):
             nn.init.normal_(m.weight, std=config.init_std)
 
-    def _heads(self, t: torch.Tensor) -> torch.Tensor:
-        return t.view(*t.shape[:-1], self.num_heads, self.head_dim)
+    def _qkv_weight(self) -> torch.Tensor:
+        return torch.cat([self.proj_q.weight, self.proj_k.weight, self.proj_v.weight], dim=0)
 
-    def _attend(self, q, k, v, pk, pv, window):
-        """q/k/v: [B, T, D]; pk/pv: [B or 1, P, D] or None -> [B, T, D] after proj_out."""
+    def _attend(self, qkv, pkv, window):
+        """qkv: [B, T, 3D]; pkv: [B or 1, P, 2D] or None -> [B, T, D] after proj_out."""
         o = window_attention(
-            self._heads(q), self._heads(k), self._heads(v),
-            None if pk is None else self._heads(pk), None if pv is None else self._heads(pv),
-            window=window, scale=self.scale,
+            qkv, pkv, self.num_heads, window=window, scale=self.scale,
             inv_freq=None if self.rope is None else self.rope.inv_freq,
             dropout_p=self.dropout.p, training=self.training, use_kernels=self.use_kernels)
-        return F.linear(o.reshape(*q.shape[:-1], self.dim), self.proj_out.weight)
+        return F.linear(o.reshape(*qkv.shape[:-1], self.dim), self.proj_out.weight)
 
 
 class SlidingWindowAttention(_AttentionBase):
@@ -108,15 +106,14 @@ class SlidingWindowAttention(_AttentionBase):
         change with it (the argument is kept for API compatibility).
         """
         del seq_offset
-        w = torch.cat([self.proj_q.weight, self.proj_k.weight, self.proj_v.weight], dim=0)
+        w = self._qkv_weight()
         qkv = F.linear(x, w)
-        D = self.dim
-        q, k, v = qkv[..., :D], qkv[..., D:2 * D], qkv[..., 2 * D:]
-        pk = pv = None
+        pkv = None
         if prefix is not None and prefix.shape[1] > 0:
-            pkv = F.linear(prefix, w[D:])
-            pk, pv = pkv[..., :D], pkv[..., D:]
-        return self._attend(q, k, v, pk, pv, self.window_size)
+            if prefix.stride(0) == 0:  # batch-broadcast persistent tokens: project once
+                prefix = prefix[:1]
+            pkv = F.linear(prefix, w[self.dim:])
+        return self._attend(qkv, pkv, self.window_size)
 
     # Mask helpers (same contract as the reference's, used by tests and debugging)
     def _create_sliding_window_mask(self, seq_len: int, device) -> torch.Tensor:
@@ -138,21 +135,21 @@ class SegmentedAttention(_AttentionBase):
                 memory: torch.Tensor | None = None) -> torch.Tensor:
         B = x.shape[0]
         D = self.dim
-        w = torch.cat([self.proj_q.weight, self.proj_k.weight, self.proj_v.weight], dim=0)
+        w = self._qkv_weight()
         qkv = F.linear(x, w)
-        q, k, v = qkv[..., :D], qkv[..., D:2 * D], qkv[..., 2 * D:]
         parts = [p for p in (persistent, memory) if p is not None and p.shape[1] > 0]
-        pk = pv = None
-        if parts:
-            if len(parts) == 2 and persistent.stride(0) == 0:
+        pkv = None
+        if len(parts) == 1:
+            pre = parts[0][:1] if parts[0].stride(0) == 0 else parts[0]
+            pkv = F.linear(pre, w[D:])
+        elif len(parts) == 2:
+            if persistent.stride(0) == 0:
                 # shared persistent rows: project once, then broadcast over the batch
                 pkv_p = F.linear(persistent[:1], w[D:]).expand(B, -1, -1)
-                pkv_m = F.linear(memory, w[D:])
-                pkv = torch.cat([pkv_p, pkv_m], dim=1)
             else:
-                pkv = F.linear(torch.cat(parts, dim=1), w[D:])
-            pk, pv = pkv[..., :D], pkv[..., D:]
-        return self._attend(q, k, v, pk, pv, None)
+                pkv_p = F.linear(persistent, w[D:])
+            pkv = torch.cat([pkv_p, F.linear(memory, w[D:])], dim=1)
+        return self._attend(qkv, pkv, None)
 
     def _create_causal_mask(self, seq_len: int, device) -> torch.Tensor:
         return torch.tril(torch.ones(seq_len, seq_len, dtype=torch.bool, device=device))[None, None]

@@ -52,15 +52,26 @@ def prefix_window_mask(q_len: int, prefix_len: int, window: int, device) -> torc
     return torch.cat([pre, main], dim=1)
 
 
-def window_attention_reference(q, k, v, pk, pv, window, scale, inv_freq, dropout_p=0.0, training=False):
-    """PyTorch restatement (dense mask + SDPA); tensors are [B, S, H, d]."""
-    B, T, H, d = q.shape
+def _split_qkv(qkv, pkv, H):
+    B, T, D3 = qkv.shape
+    D = D3 // 3
+    d = D // H
+    q, k, v = (qkv[..., i * D:(i + 1) * D].reshape(B, T, H, d) for i in range(3))
+    pk = pv = None
+    if pkv is not None and pkv.shape[1] > 0:
+        pk = pkv[..., :D].reshape(pkv.shape[0], pkv.shape[1], H, d)
+        pv = pkv[..., D:].reshape(pkv.shape[0], pkv.shape[1], H, d)
+    return q, k, v, pk, pv
+
+
+def window_attention_reference(qkv, pkv, H, window, scale, inv_freq, dropout_p=0.0, training=False):
+    """PyTorch restatement (dense mask + SDPA).  Returns [B, T, H, d]."""
+    q, k, v, pk, pv = _split_qkv(qkv, pkv, H)
+    B, T, _, d = q.shape
     P = 0 if pk is None else pk.shape[1]
     if P:
-        pk = pk.expand(B, -1, -1, -1)
-        pv = pv.expand(B, -1, -1, -1)
-        kf = torch.cat([pk, k], dim=1)
-        vf = torch.cat([pv, v], dim=1)
+        kf = torch.cat([pk.expand(B, -1, -1, -1), k], dim=1)
+        vf = torch.cat([pv.expand(B, -1, -1, -1), v], dim=1)
     else:
         kf, vf = k, v
     if inv_freq is not None:
@@ -77,44 +88,50 @@ def window_attention_reference(q, k, v, pk, pv, window, scale, inv_freq, dropout
 
 
 class _WindowAttnFn(torch.autograd.Function):
-    @staticmethod
-    def forward(ctx, q, k, v, pk, pv, window, scale, inv_freq):
-        o, lse = ext().attn_fwd(q, k, v, pk, pv, int(window), float(scale), inv_freq)
-        ctx.save_for_backward(q, k, v, pk, pv, inv_freq, o, lse)
-        ctx.window, ctx.scale = int(window), float(scale)
-        ctx.has_prefix = pk is not None
-        return o
+    """pack (RoPE + head-major layout) -> flash forward; backward -> unpack."""
 
     @staticmethod
-    def backward(ctx, do):
-        q, k, v, pk, pv, inv_freq, o, lse = ctx.saved_tensors
-        dq, dk, dv, dpk, dpv = ext().attn_bwd(do.contiguous(), q, k, v, pk, pv, o, lse,
-                                              ctx.window, ctx.scale, inv_freq)
-        if not ctx.has_prefix:
-            dpk = dpv = None
-        return dq, dk, dv, dpk, dpv, None, None, None
+    def forward(ctx, qkv, pkv, H, window, scale, inv_freq):
+        E = ext()
+        Q, K, V = E.attn_pack(qkv, pkv, H, inv_freq)
+        O, lse = E.attn_fwd_packed(Q, K, V, window, scale)
+        ctx.save_for_backward(Q, K, V, O, lse, inv_freq)
+        ctx.window, ctx.scale = window, scale
+        ctx.bp = 0 if pkv is None else pkv.shape[0]
+        ctx.dtype = qkv.dtype
+        return O
+
+    @staticmethod
+    def backward(ctx, dO):
+        Q, K, V, O, lse, inv_freq = ctx.saved_tensors
+        E = ext()
+        dQa, dKa, dVa = E.attn_bwd_packed(dO, Q, K, V, O, lse, ctx.window, ctx.scale)
+        dqkv, dpkv = E.attn_unpack(dQa, dKa, dVa, inv_freq, max(ctx.bp, 1), ctx.dtype)
+        return dqkv, (dpkv if ctx.bp else None), None, None, None, None
 
 
-def window_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
-                     pk: torch.Tensor | None = None, pv: torch.Tensor | None = None,
+def window_attention(qkv: torch.Tensor, pkv: torch.Tensor | None, num_heads: int,
                      window: int | None = None, scale: float | None = None,
                      inv_freq: torch.Tensor | None = None, dropout_p: float = 0.0,
                      training: bool = False, use_kernels: bool | None = None) -> torch.Tensor:
-    """Attention of ``q`` over ``[pk || k]`` with the prefix/window rule above.
+    """Attention of the queries in ``qkv`` over ``[prefix || main]`` keys.
 
-    Shapes: ``q, k, v`` are ``[B, T, H, d]`` (the head dim must be contiguous;
-    rows may be strided, e.g. slices of a fused QKV projection); ``pk, pv`` are
-    ``[B or 1, P, H, d]`` or ``None``.  ``window=None`` means no window (MAC).
-    Returns ``[B, T, H, d]`` contiguous.
+    ``qkv`` is the fused projection ``[B, T, 3D]`` (q | k | v, last dim
+    contiguous); ``pkv`` the projected prefix ``[B or 1, P, 2D]`` (k | v) or
+    ``None``.  ``window=None`` means no window (MAC).  Returns ``[B, T, H, d]``.
     """
     window = NO_WINDOW if window is None else int(window)
-    scale = (q.shape[-1] ** -0.5) if scale is None else scale
-    if want_kernels(q, use_kernels):
+    H = int(num_heads)
+    d = qkv.shape[-1] // 3 // H
+    scale = (d ** -0.5) if scale is None else float(scale)
+    if pkv is not None and pkv.shape[1] == 0:
+        pkv = None
+    if want_kernels(qkv, use_kernels):
         if dropout_p > 0.0 and training:
             raise NotImplementedError("attention-probability dropout is not implemented in the "
                                       "sm_100a attention kernel; set dropout=0")
-        return _WindowAttnFn.apply(q, k, v, pk, pv, window, scale, inv_freq)
-    return window_attention_reference(q, k, v, pk, pv, window, scale, inv_freq, dropout_p, training)
+        return _WindowAttnFn.apply(qkv, pkv, H, window, scale, inv_freq)
+    return window_attention_reference(qkv, pkv, H, window, scale, inv_freq, dropout_p, training)
 
 
 def attention_flops(B: int, T: int, H: int, d: int, P: int, window: int | None) -> float:

@@ -124,10 +124,59 @@ def memory_step(k: torch.Tensor, v: torch.Tensor, x_for_gates: torch.Tensor,
     state, `memory.py:330-331, 461`).
     """
     if want_kernels(k, use_kernels):
-        return ext().memory_step(k, v, x_for_gates, list(weights), list(momentum),
-                                 list(gate_ws), list(gate_bs), float(lr), float(mom), act,
-                                 bool(linear_silu))
+        return _memory_step_cuda(k, v, x_for_gates, weights, momentum, gate_ws, gate_bs,
+                                 lr, mom, act, linear_silu)
     x_mean = x_for_gates.float().mean(dim=1, keepdim=True).to(x_for_gates.dtype)
     alpha, theta, eta = memory_gates_reference(x_mean, gate_ws, gate_bs, lr, mom)
     grads = memory_grads_reference(k, v, weights, act, linear_silu)
     return memory_update_reference(weights, momentum, grads, alpha, eta, theta)
+
+
+def _memory_step_cuda(k, v, x_for_gates, weights, momentum, gate_ws, gate_bs, lr, mom, act,
+                      linear_silu):
+    """Device-resident update: gates kernel, cuBLAS GEMMs with fp32 weight-grad
+    output, activation/error epilogue kernels, fused momentum/decay update."""
+    E = ext()
+    gates = E.memory_gates(x_for_gates, list(gate_ws), list(gate_bs), float(lr), float(mom))
+    B, T, D = k.shape
+    k2 = k.reshape(-1, D)
+    v2 = v.reshape(-1, v.shape[-1])
+    if not k2.is_contiguous():
+        k2 = k2.contiguous()
+    if not v2.is_contiguous():
+        v2 = v2.contiguous()
+    L = len(weights)
+    if L == 1 and linear_silu:
+        h = torch.empty_like(k2)
+        E.act_inplace(k2, h, act)
+        pred = torch.mm(h, weights[0].t())
+        E.scaled_err(pred, v2, 2.0 / (B * T))
+        grads = [torch.mm(pred.t(), h, out_dtype=torch.float32)]
+    else:
+        hs, zs = [k2], []
+        h = k2
+        for i, w in enumerate(weights):
+            z = torch.mm(h, w.t())
+            if i < L - 1:
+                a = torch.empty_like(z)
+                E.act_inplace(z, a, act)
+                zs.append(z)
+                hs.append(a)
+                h = a
+            else:
+                h = z
+        E.scaled_err(h, v2, 2.0 / h.numel())
+        delta = h
+        grads = [None] * L
+        for i in range(L - 1, -1, -1):
+            grads[i] = torch.mm(delta.t(), hs[i], out_dtype=torch.float32)
+            if i > 0:
+                nd = torch.mm(delta, weights[i])
+                E.act_grad_mul(nd, zs[i - 1], act)
+                delta = nd
+    new_w, new_m = [], []
+    for w, m, g in zip(weights, momentum, grads, strict=True):
+        w2, m2 = E.mem_update(w, m, g, gates)
+        new_w.append(w2)
+        new_m.append(m2)
+    return new_w, new_m

@@ -1,0 +1,124 @@
+"""Training step / loop for Titans models.
+
+Mirrors the reference trainer's step (`scripts/pretrain.py:559-625`): forward,
+mean token cross-entropy, backward, global-norm clip, AdamW(beta=(0.9, 0.95)),
+LR schedule (linear warm-up then cosine to a 0.1 floor, `:408-425`).  The
+differences are the B200 ones: the model computes in bf16 with fp32 master
+weights held by :class:`FusedAdamW`; clip and update are device kernels; the
+loss stays on the device until the caller asks for it; with a process group,
+gradients are reduced by the data-parallel engine before the update.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+
+from ..ops.loss import cross_entropy
+from .optim import FusedAdamW
+
+
+def cosine_with_warmup(step: int, warmup: int, total: int, min_ratio: float = 0.1) -> float:
+    """LR multiplier: linear warm-up, then cosine decay to ``min_ratio``."""
+    if step < warmup:
+        return float(step) / float(max(1, warmup))
+    progress = float(step - warmup) / float(max(1, total - warmup))
+    return max(min_ratio, 0.5 * (1.0 + math.cos(math.pi * progress)))
+
+
+def get_cosine_schedule_with_warmup(optimizer, num_warmup_steps: int, num_training_steps: int,
+                                    min_lr_ratio: float = 0.1):
+    return torch.optim.lr_scheduler.LambdaLR(
+        optimizer, lambda s: cosine_with_warmup(s, num_warmup_steps, num_training_steps, min_lr_ratio))
+
+
+@dataclass
+class TrainStepConfig:
+    lr: float = 4e-4
+    weight_decay: float = 0.1
+    betas: tuple[float, float] = (0.9, 0.95)
+    eps: float = 1e-8
+    grad_clip: float = 1.0
+    warmup_steps: int = 0
+    total_steps: int = 0          # 0: constant LR after warm-up
+    min_lr_ratio: float = 0.1
+    gradient_accumulation_steps: int = 1
+    dtype: torch.dtype = torch.bfloat16
+
+
+class Trainer:
+    """One-GPU (or data-parallel, see ``engine``) training driver."""
+
+    def __init__(self, model: torch.nn.Module, cfg: TrainStepConfig | None = None,
+                 device: torch.device | str | None = None, engine=None) -> None:
+        self.cfg = cfg or TrainStepConfig()
+        if device is None:
+            device = torch.device("cuda") if torch.cuda.is_available() else torch.device("cpu")
+        self.device = torch.device(device)
+        self.model = model.to(device=self.device, dtype=self.cfg.dtype)
+        self.engine = engine
+        if engine is not None:
+            self.optimizer = engine.make_optimizer(self.model, self.cfg)
+        else:
+            self.optimizer = FusedAdamW(self.model.parameters(), lr=self.cfg.lr, betas=self.cfg.betas,
+                                        eps=self.cfg.eps, weight_decay=self.cfg.weight_decay,
+                                        max_grad_norm=self.cfg.grad_clip,
+                                        use_kernels=getattr(self.model.config, "use_kernels", None))
+        self.scheduler = None
+        if self.cfg.total_steps > 0 or self.cfg.warmup_steps > 0:
+            self.scheduler = get_cosine_schedule_with_warmup(
+                self.optimizer, self.cfg.warmup_steps, max(self.cfg.total_steps, 1), self.cfg.min_lr_ratio)
+        self.global_step = 0
+        self._micro = 0
+        self.optimizer.zero_grad()
+
+    def _to_device(self, t: torch.Tensor) -> torch.Tensor:
+        return t.to(self.device, non_blocking=True)
+
+    def loss_fn(self, input_ids: torch.Tensor, labels: torch.Tensor) -> torch.Tensor:
+        logits, _ = self.model(input_ids)
+        return cross_entropy(logits, labels, use_kernels=getattr(self.model.config, "use_kernels", None))
+
+    def train_step(self, batch: dict[str, torch.Tensor]) -> torch.Tensor:
+        """Forward + backward (+ optimizer step at accumulation boundaries).
+
+        ``batch`` holds ``input_ids`` and ``labels`` (host or device tensors).
+        Returns the micro-batch loss as a device tensor (no host sync).
+        """
+        self.model.train()
+        ids = self._to_device(batch["input_ids"])
+        labels = self._to_device(batch["labels"])
+        accum = self.cfg.gradient_accumulation_steps
+        loss = self.loss_fn(ids, labels)
+        (loss / accum if accum > 1 else loss).backward()
+        self._micro += 1
+        if self._micro % accum == 0:
+            self.optimizer_step()
+        return loss.detach()
+
+    def optimizer_step(self) -> None:
+        if self.engine is not None:
+            self.engine.reduce_gradients(self.optimizer)
+        self.optimizer.step()
+        if self.scheduler is not None:
+            self.scheduler.step()
+        self.optimizer.zero_grad()
+        self.global_step += 1
+
+    @torch.no_grad()
+    def evaluate(self, batches) -> dict[str, float]:
+        self.model.eval()
+        tot, n = 0.0, 0
+        for b in batches:
+            ids = self._to_device(b["input_ids"])
+            labels = self._to_device(b["labels"])
+            logits, _ = self.model(ids)
+            loss = cross_entropy(logits, labels)
+            k = int((labels != -100).sum())
+            tot += float(loss) * k
+            n += k
+        self.model.train()
+        avg = tot / max(n, 1)
+        return {"val_loss": avg, "val_ppl": math.exp(min(avg, 20.0))}

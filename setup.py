@@ -40,7 +40,6 @@ setup(
             sources=sources,
             include_dirs=[os.path.join(HERE, CSRC)],
             extra_compile_args={"cxx": ["-O3", "-std=c++17"], "nvcc": nvcc_flags},
-            libraries=["cuda"],
         )
     ],
     cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},

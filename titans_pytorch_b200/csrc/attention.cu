@@ -84,43 +84,85 @@ __device__ __forceinline__ bool visible(int i, int j, int P, int Tn, int W) {
   return jm < Tn && jm <= i && (i - jm) < W;
 }
 
+// 8 consecutive elements as floats (one 16-byte access for 16-bit types, two for fp32)
+template <typename T>
+__device__ __forceinline__ void load8(const T* p, float (&o)[8]) {
+  if constexpr (sizeof(T) == 2) {
+    load16<T>(p, o);
+  } else {
+    float a[4], b[4];
+    load16<T>(p, a);
+    load16<T>(p + 4, b);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) { o[i] = a[i]; o[4 + i] = b[i]; }
+  }
+}
+template <typename T>
+__device__ __forceinline__ void store8(T* p, const float (&o)[8]) {
+  if constexpr (sizeof(T) == 2) {
+    store16<T>(p, o);
+  } else {
+    float a[4] = {o[0], o[1], o[2], o[3]}, b[4] = {o[4], o[5], o[6], o[7]};
+    store16<T>(p, a);
+    store16<T>(p + 4, b);
+  }
+}
+__device__ __forceinline__ void load8f(const float* p, float (&o)[8]) {
+  const float4 a = *reinterpret_cast<const float4*>(p), b = *reinterpret_cast<const float4*>(p + 4);
+  o[0] = a.x; o[1] = a.y; o[2] = a.z; o[3] = a.w; o[4] = b.x; o[5] = b.y; o[6] = b.z; o[7] = b.w;
+}
+
+// rotate 4 interleaved pairs at position pos (pair indices p0..p0+3); sgn = -1 inverts
+__device__ __forceinline__ void rope8(float (&v)[8], const float* inv_freq, int p0, float pos, float sgn) {
+  if (inv_freq == nullptr) return;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    float sn, cs;
+    sincosf(pos * inv_freq[p0 + q], &sn, &cs);
+    sn *= sgn;
+    const float a = v[2 * q], b = v[2 * q + 1];
+    v[2 * q] = a * cs - b * sn;
+    v[2 * q + 1] = a * sn + b * cs;
+  }
+}
+
 // ------------------------------------------------------------------ pack
-// qkv: [B, T, 3D] (row stride sr, batch stride sb); pkv: [Bp, P, 2D] contiguous
+// qkv: [B, T, 3D] (row stride sr, batch stride sb); pkv: [Bp, P, 2D] contiguous.
+// One work item = 8 consecutive head-dim elements of one (b, key row j, head h).
 template <typename T>
 __global__ void pack_kernel(const T* __restrict__ qkv, int64_t sb, int64_t sr, const T* __restrict__ pkv, int Bp,
                             const float* __restrict__ inv_freq, bf16* __restrict__ Q, bf16* __restrict__ K,
                             bf16* __restrict__ V, int B, int Tn, int P, int H, int HD) {
   const int D = H * HD;
-  const int half = HD / 2;
-  const int64_t total = (int64_t)B * (P + Tn) * H * half;
+  const int cpr = HD / 8;
+  const int64_t total = (int64_t)B * (P + Tn) * H * cpr;
   for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
-    const int pi = (int)(e % half);
-    int64_t r = e / half;
+    const int c = (int)(e % cpr);
+    int64_t r = e / cpr;
     const int h = (int)(r % H);
     r /= H;
     const int j = (int)(r % (P + Tn));  // combined key row
     const int b = (int)(r / (P + Tn));
-    float c = 1.f, s = 0.f;
-    if (inv_freq) sincosf((float)j * inv_freq[pi], &s, &c);
-    const int64_t kidx = (((int64_t)b * H + h) * (P + Tn) + j) * HD + 2 * pi;
-    const T *kp, *vp;
+    const int col = h * HD + c * 8;
+    const int64_t kidx = (((int64_t)b * H + h) * (P + Tn) + j) * HD + c * 8;
+    float k[8], v[8];
     if (j < P) {
       const T* row = pkv + ((int64_t)(Bp == 1 ? 0 : b) * P + j) * 2 * D;
-      kp = row + h * HD + 2 * pi;
-      vp = row + D + h * HD + 2 * pi;
+      load8<T>(row + col, k);
+      load8<T>(row + D + col, v);
     } else {
       const T* row = qkv + (int64_t)b * sb + (int64_t)(j - P) * sr;
-      kp = row + D + h * HD + 2 * pi;
-      vp = row + 2 * D + h * HD + 2 * pi;
-      // query at main position i = j - P has rope position P + i = j
-      const T* qp = row + h * HD + 2 * pi;
-      const float q0 = to_f<T>(qp[0]), q1 = to_f<T>(qp[1]);
-      const int64_t qidx = (((int64_t)b * H + h) * Tn + (j - P)) * HD + 2 * pi;
-      *reinterpret_cast<__nv_bfloat162*>(Q + qidx) = __floats2bfloat162_rn(q0 * c - q1 * s, q0 * s + q1 * c);
+      float q[8];
+      load8<T>(row + col, q);
+      load8<T>(row + D + col, k);
+      load8<T>(row + 2 * D + col, v);
+      // the query at main position i = j - P has rope position P + i = j
+      rope8(q, inv_freq, c * 4, (float)j, 1.f);
+      store8<bf16>(Q + (((int64_t)b * H + h) * Tn + (j - P)) * HD + c * 8, q);
     }
-    const float k0 = to_f<T>(kp[0]), k1 = to_f<T>(kp[1]);
-    *reinterpret_cast<__nv_bfloat162*>(K + kidx) = __floats2bfloat162_rn(k0 * c - k1 * s, k0 * s + k1 * c);
-    *reinterpret_cast<__nv_bfloat162*>(V + kidx) = __floats2bfloat162_rn(to_f<T>(vp[0]), to_f<T>(vp[1]));
+    rope8(k, inv_freq, c * 4, (float)j, 1.f);
+    store8<bf16>(K + kidx, k);
+    store8<bf16>(V + kidx, v);
   }
 }
 
@@ -131,57 +173,53 @@ __global__ void unpack_kernel(const float* __restrict__ dQa, const float* __rest
                               const float* __restrict__ dVa, const float* __restrict__ inv_freq, T* __restrict__ dqkv,
                               T* __restrict__ dpkv, int Bp, int B, int Tn, int P, int H, int HD) {
   const int D = H * HD;
-  const int half = HD / 2;
-  // main rows: one work item per (b, t, h, pair)
-  const int64_t total_main = (int64_t)B * Tn * H * half;
-  const int64_t total_pre = (int64_t)Bp * P * H * half;
+  const int cpr = HD / 8;
+  const int64_t total_main = (int64_t)B * Tn * H * cpr;
+  const int64_t total_pre = (int64_t)Bp * P * H * cpr;
   for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total_main + total_pre;
        e += (int64_t)gridDim.x * blockDim.x) {
     if (e < total_main) {
-      const int pi = (int)(e % half);
-      int64_t r = e / half;
+      const int c = (int)(e % cpr);
+      int64_t r = e / cpr;
       const int h = (int)(r % H);
       r /= H;
       const int t = (int)(r % Tn);
       const int b = (int)(r / Tn);
       const int j = P + t;
-      float c = 1.f, s = 0.f;
-      if (inv_freq) sincosf((float)j * inv_freq[pi], &s, &c);
       const int64_t bh = (int64_t)b * H + h;
-      const float2 dq = *reinterpret_cast<const float2*>(dQa + (bh * Tn + t) * HD + 2 * pi);
-      const float2 dk = *reinterpret_cast<const float2*>(dKa + (bh * (P + Tn) + j) * HD + 2 * pi);
-      const float2 dv = *reinterpret_cast<const float2*>(dVa + (bh * (P + Tn) + j) * HD + 2 * pi);
-      T* row = dqkv + ((int64_t)b * Tn + t) * 3 * D + h * HD + 2 * pi;
+      float dq[8], dk[8], dv[8];
+      load8f(dQa + (bh * Tn + t) * HD + c * 8, dq);
+      load8f(dKa + (bh * (P + Tn) + j) * HD + c * 8, dk);
+      load8f(dVa + (bh * (P + Tn) + j) * HD + c * 8, dv);
       // inverse rotation: R(-a) applied to the gradient of the rotated vector
-      row[0] = from_f<T>(dq.x * c + dq.y * s);
-      row[1] = from_f<T>(-dq.x * s + dq.y * c);
-      row[D] = from_f<T>(dk.x * c + dk.y * s);
-      row[D + 1] = from_f<T>(-dk.x * s + dk.y * c);
-      row[2 * D] = from_f<T>(dv.x);
-      row[2 * D + 1] = from_f<T>(dv.y);
+      rope8(dq, inv_freq, c * 4, (float)j, -1.f);
+      rope8(dk, inv_freq, c * 4, (float)j, -1.f);
+      T* row = dqkv + ((int64_t)b * Tn + t) * 3 * D + h * HD + c * 8;
+      store8<T>(row, dq);
+      store8<T>(row + D, dk);
+      store8<T>(row + 2 * D, dv);
     } else {
       const int64_t e2 = e - total_main;
-      const int pi = (int)(e2 % half);
-      int64_t r = e2 / half;
+      const int c = (int)(e2 % cpr);
+      int64_t r = e2 / cpr;
       const int h = (int)(r % H);
       r /= H;
       const int j = (int)(r % P);
       const int bp = (int)(r / P);
-      float c = 1.f, s = 0.f;
-      if (inv_freq) sincosf((float)j * inv_freq[pi], &s, &c);
-      float kx = 0.f, ky = 0.f, vx = 0.f, vy = 0.f;
+      float kx[8] = {0, 0, 0, 0, 0, 0, 0, 0}, vx[8] = {0, 0, 0, 0, 0, 0, 0, 0};
       const int b_lo = Bp == 1 ? 0 : bp, b_hi = Bp == 1 ? B : bp + 1;
       for (int b = b_lo; b < b_hi; ++b) {
-        const int64_t base = (((int64_t)b * H + h) * (P + Tn) + j) * HD + 2 * pi;
-        const float2 dk = *reinterpret_cast<const float2*>(dKa + base);
-        const float2 dv = *reinterpret_cast<const float2*>(dVa + base);
-        kx += dk.x; ky += dk.y; vx += dv.x; vy += dv.y;
+        const int64_t base = (((int64_t)b * H + h) * (P + Tn) + j) * HD + c * 8;
+        float dk[8], dv[8];
+        load8f(dKa + base, dk);
+        load8f(dVa + base, dv);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) { kx[i] += dk[i]; vx[i] += dv[i]; }
       }
-      T* row = dpkv + ((int64_t)bp * P + j) * 2 * D + h * HD + 2 * pi;
-      row[0] = from_f<T>(kx * c + ky * s);
-      row[1] = from_f<T>(-kx * s + ky * c);
-      row[D] = from_f<T>(vx);
-      row[D + 1] = from_f<T>(vy);
+      rope8(kx, inv_freq, c * 4, (float)j, -1.f);
+      T* row = dpkv + ((int64_t)bp * P + j) * 2 * D + h * HD + c * 8;
+      store8<T>(row, kx);
+      store8<T>(row + D, vx);
     }
   }
 }
@@ -390,28 +428,41 @@ __global__ void __launch_bounds__(128) attn_fwd_kernel(const bf16* __restrict__ 
 }
 
 // ------------------------------------------------------------ backward pre
-// Dd[bh, i] = sum_d dO[b,i,h,d] * O[b,i,h,d];  also converts LSE to log2 units
+// Dd[bh, i] = sum_d dO[b,i,h,d] * O[b,i,h,d]; also converts LSE to log2 units.
+// A group of HD/8 consecutive threads handles one row with 16-byte loads.
 __global__ void bwd_pre_kernel(const bf16* __restrict__ dO, const bf16* __restrict__ O, const float* __restrict__ LSE,
                                float* __restrict__ Dd, float* __restrict__ LSE2, int B, int H, int Tn, int HD) {
+  const int cpr = HD / 8;  // 4, 8, 12 or 16 threads per row
   const int64_t rows = (int64_t)B * H * Tn;
-  const int lane = threadIdx.x & 31;
-  const int64_t w0 = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  const int64_t nw = (int64_t)gridDim.x * (blockDim.x >> 5);
-  for (int64_t r = w0; r < rows; r += nw) {
-    const int i = (int)(r % Tn);
-    const int64_t bh = r / Tn;
-    const int b = (int)(bh / H), h = (int)(bh % H);
-    const int64_t off = (((int64_t)b * Tn + i) * H + h) * HD;
+  const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  // every thread runs the same number of steps so the shuffles below stay convergent
+  const int64_t nsteps = (rows * cpr + stride - 1) / stride;
+  for (int64_t s = 0; s < nsteps; ++s) {
+    const int64_t e = tid + s * stride;
+    const int64_t r = e / cpr;
+    const int c = (int)(e % cpr);
     float acc = 0.f;
-    for (int d = lane * 2; d < HD; d += 64) {
-      const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(dO + off + d));
-      const float2 c = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(O + off + d));
-      acc += a.x * c.x + a.y * c.y;
+    if (r < rows) {
+      const int i = (int)(r % Tn);
+      const int64_t bh = r / Tn;
+      const int b = (int)(bh / H), h = (int)(bh % H);
+      const int64_t off = (((int64_t)b * Tn + i) * H + h) * HD + c * 8;
+      float a[8], o[8];
+      load16<bf16>(dO + off, a);
+      load16<bf16>(O + off, o);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) acc += a[k] * o[k];
     }
-    acc = warp_sum(acc);
-    if (lane == 0) {
-      Dd[r] = acc;
-      LSE2[r] = LSE[r] * 1.4426950408889634f;
+    if ((32 % cpr) == 0) {  // a row's group lies inside one warp
+      for (int o2 = 1; o2 < cpr; o2 <<= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o2);
+      if (r < rows && c == 0) {
+        Dd[r] = acc;
+        LSE2[r] = LSE[r] * 1.4426950408889634f;
+      }
+    } else if (r < rows) {  // head_dim 96: groups of 12 straddle warps
+      atomicAdd(Dd + r, acc);
+      if (c == 0) LSE2[r] = LSE[r] * 1.4426950408889634f;
     }
   }
 }
@@ -685,8 +736,9 @@ std::vector<at::Tensor> attn_pack(const at::Tensor& qkv, const c10::optional<at:
   at::Tensor Q = at::empty({B, H, Tn, HD}, opts);
   at::Tensor K = at::empty({B, H, P + Tn, HD}, opts);
   at::Tensor V = at::empty({B, H, P + Tn, HD}, opts);
-  const int64_t total = (int64_t)B * (P + Tn) * H * (HD / 2);
+  const int64_t total = (int64_t)B * (P + Tn) * H * (HD / 8);
   if (total == 0) return {Q, K, V};
+  TORCH_CHECK(qkv.stride(1) % 8 == 0 && qkv.stride(0) % 8 == 0 && aligned16(qkv), "attn_pack: qkv alignment");
   const int blocks = (int)std::min<int64_t>((total + 255) / 256, (int64_t)num_sms() * 16);
   TB_DISPATCH_FLOAT(qkv.scalar_type(), "attn_pack", [&] {
     attn::pack_kernel<scalar_t><<<blocks, 256, 0, stream()>>>(
@@ -739,11 +791,11 @@ std::vector<at::Tensor> attn_bwd_packed(const at::Tensor& dO_in, const at::Tenso
   at::Tensor dKa = at::zeros({B, H, P + Tn, HD}, f32);
   at::Tensor dVa = at::zeros({B, H, P + Tn, HD}, f32);
   if (B * H * Tn == 0) return {dQa, dKa, dVa};
-  at::Tensor Dd = at::empty({B, H, Tn}, f32);
+  at::Tensor Dd = (32 % (HD / 8) == 0) ? at::empty({B, H, Tn}, f32) : at::zeros({B, H, Tn}, f32);
   at::Tensor L2 = at::empty({B, H, Tn}, f32);
   {
-    const int64_t rows = (int64_t)B * H * Tn;
-    const int blocks = (int)std::min<int64_t>((rows + 7) / 8, (int64_t)num_sms() * 16);
+    const int64_t work = (int64_t)B * H * Tn * (HD / 8);
+    const int blocks = (int)std::min<int64_t>((work + 255) / 256, (int64_t)num_sms() * 16);
     attn::bwd_pre_kernel<<<blocks, 256, 0, stream()>>>((const bf16*)dO.data_ptr(), (const bf16*)O.data_ptr(),
                                                        LSE.data_ptr<float>(), Dd.data_ptr<float>(),
                                                        L2.data_ptr<float>(), B, H, Tn, HD);
@@ -781,7 +833,7 @@ std::vector<at::Tensor> attn_unpack(const at::Tensor& dQa, const at::Tensor& dKa
   auto opts = dQa.options().dtype(dtype);
   at::Tensor dqkv = at::empty({B, Tn, 3 * D}, opts);
   at::Tensor dpkv = at::empty({P ? Bp : 0, P, 2 * D}, opts);
-  const int64_t total = (int64_t)B * Tn * H * (HD / 2) + (int64_t)(P ? Bp : 0) * P * H * (HD / 2);
+  const int64_t total = (int64_t)B * Tn * H * (HD / 8) + (int64_t)(P ? Bp : 0) * P * H * (HD / 8);
   if (total == 0) return {dqkv, dpkv};
   const int blocks = (int)std::min<int64_t>((total + 255) / 256, (int64_t)num_sms() * 16);
   TB_DISPATCH_FLOAT(dtype, "attn_unpack", [&] {

@@ -45,6 +45,11 @@ std::vector<at::Tensor> attn_bwd_packed(const at::Tensor& dO, const at::Tensor& 
                                         int64_t window, double scale);
 std::vector<at::Tensor> attn_unpack(const at::Tensor& dQa, const at::Tensor& dKa, const at::Tensor& dVa,
                                     const c10::optional<at::Tensor>& inv_freq, int64_t Bp, at::ScalarType dtype);
+// attention_tc.cu
+std::vector<at::Tensor> attn_fwd_tc(const at::Tensor& Q, const at::Tensor& K, const at::Tensor& V, int64_t window,
+                                    double scale);
+bool attn_tc_supported(int64_t head_dim);
+int64_t kernel_error_status(int64_t device, bool reset);
 }  // namespace tb
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -68,4 +73,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_fwd_packed", &tb::attn_fwd_packed);
   m.def("attn_bwd_packed", &tb::attn_bwd_packed);
   m.def("attn_unpack", &tb::attn_unpack);
+  m.def("attn_fwd_tc", &tb::attn_fwd_tc);
+  m.def("attn_tc_supported", &tb::attn_tc_supported);
+  m.def("kernel_error_status", &tb::kernel_error_status, pybind11::arg("device") = 0, pybind11::arg("reset") = true);
 }

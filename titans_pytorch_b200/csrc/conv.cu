@@ -1,242 +1,219 @@
 // Causal depthwise conv1d + bias + SiLU (+ row L2-normalisation), forward and
-// backward.  Forward: one warp per (b, t) row reads the K input rows it needs
-// (neighbouring warps share them through L1/L2) and writes the finished row.
-// Backward: kernel A recomputes the forward for a row and writes dc, the
-// gradient at the conv output (fp32); kernel B (column slabs x row groups)
-// forms dx by the transposed convolution of dc and accumulates dw/db partials
-// in registers, reduced in a fixed order (deterministic).
+// backward, written for memory-level parallelism.
+//
+// Forward / backward-A: a thread owns one (row, 16-byte column slice); the K
+// input rows it needs are independent loads (clamped address, zeroed when
+// before t = 0), so all of them are in flight at once and neighbouring rows'
+// re-reads hit L1/L2.  A block is RB rows x TPR threads (TPR = the threads of
+// one row, a multiple of 32), so the per-row L2-norm reduction is a warp
+// shuffle plus a few shared-memory adds.
+//
+// Backward-B: dx by the transposed convolution of dc, and the dw/db column
+// sums; each thread walks a time range U rows at a time with all 2*(U+K-1)
+// loads of a step issued before any use, keeping the partial sums in
+// registers; block partials are reduced in a fixed order (deterministic).
 #include "common.cuh"
 
 namespace tb {
 
 constexpr float kL2Eps = 1e-12f;  // F.normalize default eps
 
-template <typename T>
-__device__ __forceinline__ void load4(const T* p, float (&o)[4]) {
-  if constexpr (sizeof(T) == 4) {
-    float4 v = *reinterpret_cast<const float4*>(p);
-    o[0] = v.x; o[1] = v.y; o[2] = v.z; o[3] = v.w;
-  } else {
-    union { uint2 r; T h[4]; } u;
-    u.r = *reinterpret_cast<const uint2*>(p);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) o[i] = to_f<T>(u.h[i]);
-  }
-}
-template <typename T>
-__device__ __forceinline__ void store4(T* p, const float (&o)[4]) {
-  if constexpr (sizeof(T) == 4) {
-    *reinterpret_cast<float4*>(p) = make_float4(o[0], o[1], o[2], o[3]);
-  } else {
-    union { uint2 r; T h[4]; } u;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) u.h[i] = from_f<T>(o[i]);
-    *reinterpret_cast<uint2*>(p) = u.r;
-  }
-}
-
-// wt: [K, D] fp32 (transposed weights) or null; bias: [D] fp32 or null.
-template <typename T, int CH>
-__global__ void __launch_bounds__(256) conv_fwd_kernel(const T* __restrict__ x, int64_t sb, int64_t st,
-                                                       const float* __restrict__ wt, const float* __restrict__ bias,
-                                                       T* __restrict__ y, int B, int Tn, int D, int K, bool normalize) {
-  const int lane = threadIdx.x & 31;
-  const int64_t rows = (int64_t)B * Tn;
-  const int64_t warp0 = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
-  for (int64_t r = warp0; r < rows; r += nwarps) {
-    const int b = (int)(r / Tn), t = (int)(r % Tn);
-    const T* xb = x + (int64_t)b * sb;
-    float v[CH][4];
-    float ss = 0.f;
-#pragma unroll
-    for (int c = 0; c < CH; ++c) {
-      const int col = (c * 32 + lane) * 4;
-      if (col < D) {
-        float acc[4];
-        if (wt != nullptr) {
-#pragma unroll
-          for (int i = 0; i < 4; ++i) acc[i] = bias ? bias[col + i] : 0.f;
-          for (int j = 0; j < K; ++j) {
-            const int tt = t - K + 1 + j;
-            if (tt < 0) continue;
-            float xv[4];
-            load4<T>(xb + (int64_t)tt * st + col, xv);
-            const float4 ww = *reinterpret_cast<const float4*>(wt + (int64_t)j * D + col);
-            acc[0] += ww.x * xv[0]; acc[1] += ww.y * xv[1]; acc[2] += ww.z * xv[2]; acc[3] += ww.w * xv[3];
-          }
-        } else {
-          load4<T>(xb + (int64_t)t * st + col, acc);
-        }
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          v[c][i] = silu_(acc[i]);
-          ss += v[c][i] * v[c][i];
-        }
-      }
-    }
-    float inv = 1.f;
-    if (normalize) inv = 1.f / fmaxf(sqrtf(warp_sum(ss)), kL2Eps);
-    T* yr = y + r * D;
-#pragma unroll
-    for (int c = 0; c < CH; ++c) {
-      const int col = (c * 32 + lane) * 4;
-      if (col < D) {
-#pragma unroll
-        for (int i = 0; i < 4; ++i) v[c][i] *= inv;
-        store4<T>(yr + col, v[c]);
-      }
-    }
-  }
-}
-
-// Kernel A: dc = d(loss)/d(conv output), fp32 [B*T, D]; when there is no conv
-// it writes dx (type T) directly.
-template <typename T, int CH>
-__global__ void __launch_bounds__(256) conv_bwd_a_kernel(const T* __restrict__ dy, const T* __restrict__ x,
-                                                         int64_t sb, int64_t st, const float* __restrict__ wt,
-                                                         const float* __restrict__ bias, float* __restrict__ dc,
-                                                         T* __restrict__ dx_direct, int B, int Tn, int D, int K,
-                                                         bool normalize) {
-  const int lane = threadIdx.x & 31;
-  const int64_t rows = (int64_t)B * Tn;
-  const int64_t warp0 = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
-  for (int64_t r = warp0; r < rows; r += nwarps) {
-    const int b = (int)(r / Tn), t = (int)(r % Tn);
-    const T* xb = x + (int64_t)b * sb;
-    float pre[CH][4], s[CH][4], g[CH][4];
-    float ss = 0.f, sd = 0.f;
-#pragma unroll
-    for (int c = 0; c < CH; ++c) {
-      const int col = (c * 32 + lane) * 4;
-      if (col < D) {
-        if (wt != nullptr) {
-#pragma unroll
-          for (int i = 0; i < 4; ++i) pre[c][i] = bias ? bias[col + i] : 0.f;
-          for (int j = 0; j < K; ++j) {
-            const int tt = t - K + 1 + j;
-            if (tt < 0) continue;
-            float xv[4];
-            load4<T>(xb + (int64_t)tt * st + col, xv);
-            const float4 ww = *reinterpret_cast<const float4*>(wt + (int64_t)j * D + col);
-            pre[c][0] += ww.x * xv[0]; pre[c][1] += ww.y * xv[1]; pre[c][2] += ww.z * xv[2]; pre[c][3] += ww.w * xv[3];
-          }
-        } else {
-          load4<T>(xb + (int64_t)t * st + col, pre[c]);
-        }
-        load4<T>(dy + r * D + col, g[c]);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          s[c][i] = silu_(pre[c][i]);
-          ss += s[c][i] * s[c][i];
-        }
-      }
-    }
-    if (normalize) {
-      const float nrm = sqrtf(warp_sum(ss));
-      const float den = fmaxf(nrm, kL2Eps);
-      // y = s / den; for nrm > eps: ds = (g - y (y.g)) / den ; else ds = g / eps
-      if (nrm > kL2Eps) {
-#pragma unroll
-        for (int c = 0; c < CH; ++c) {
-          const int col = (c * 32 + lane) * 4;
-          if (col < D)
-#pragma unroll
-            for (int i = 0; i < 4; ++i) sd += s[c][i] * g[c][i];
-        }
-        sd = warp_sum(sd) / (den * den);
-      }
-#pragma unroll
-      for (int c = 0; c < CH; ++c)
-#pragma unroll
-        for (int i = 0; i < 4; ++i) g[c][i] = (g[c][i] - s[c][i] * sd) / den;
-    }
-#pragma unroll
-    for (int c = 0; c < CH; ++c) {
-      const int col = (c * 32 + lane) * 4;
-      if (col < D) {
-        float o[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) o[i] = g[c][i] * silu_grad_(pre[c][i]);
-        if (dc != nullptr) {
-          *reinterpret_cast<float4*>(dc + r * D + col) = make_float4(o[0], o[1], o[2], o[3]);
-        } else {
-          store4<T>(dx_direct + (int64_t)b * Tn * D + (int64_t)t * D + col, o);
-        }
-      }
-    }
-  }
-}
-
-// Kernel B: grid (D/128 column slabs, row groups); block 8 warps.
-template <typename T>
-__global__ void __launch_bounds__(256) conv_bwd_b_kernel(const float* __restrict__ dc, const T* __restrict__ x,
-                                                         int64_t sb, int64_t st, const float* __restrict__ wt,
-                                                         T* __restrict__ dx, float* __restrict__ part, int B, int Tn,
-                                                         int D, int K) {
-  constexpr int KMAX = 8;
-  __shared__ float red[8][KMAX + 1][128];
-  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-  const int col = blockIdx.x * 128 + lane * 4;
-  const bool active = col < D;
-  float aw[KMAX][4], ab[4];
-#pragma unroll
-  for (int j = 0; j < KMAX; ++j)
-#pragma unroll
-    for (int i = 0; i < 4; ++i) aw[j][i] = 0.f;
-#pragma unroll
-  for (int i = 0; i < 4; ++i) ab[i] = 0.f;
-  const int64_t rows = (int64_t)B * Tn;
+template <typename T, int KS>
+__global__ void __launch_bounds__(512) conv_fwd_rows(const T* __restrict__ x, int64_t sb, int64_t st,
+                                                     const float* __restrict__ wt, const float* __restrict__ bias,
+                                                     T* __restrict__ y, int64_t rows, int Tn, int D, bool normalize) {
+  constexpr int V = Vec16<T>::N;
+  __shared__ float red[32][33];
+  const int tpr = blockDim.x, lane = threadIdx.x & 31, wir = threadIdx.x >> 5;
+  const int64_t r = (int64_t)blockIdx.x * blockDim.y + threadIdx.y;
+  const int col = threadIdx.x * V;
+  const bool active = col < D && r < rows;
+  float o[V];
+  float ss = 0.f;
   if (active) {
-    for (int64_t r = (int64_t)blockIdx.y * 8 + wid; r < rows; r += (int64_t)gridDim.y * 8) {
-      const int b = (int)(r / Tn), t = (int)(r % Tn);
-      const float4 g4 = *reinterpret_cast<const float4*>(dc + r * D + col);
-      const float g[4] = {g4.x, g4.y, g4.z, g4.w};
-      ab[0] += g[0]; ab[1] += g[1]; ab[2] += g[2]; ab[3] += g[3];
-      const T* xb = x + (int64_t)b * sb;
-      float o[4] = {0.f, 0.f, 0.f, 0.f};
+    const int b = (int)(r / Tn), t = (int)(r % Tn);
+    const T* xb = x + (int64_t)b * sb + col;
+    float xv[KS][V];
 #pragma unroll
-      for (int j = 0; j < KMAX; ++j) {
-        if (j >= K) break;
-        // dw[d, j] += dc[t, d] * x[t - K + 1 + j, d]
-        const int tt = t - K + 1 + j;
-        if (tt >= 0) {
-          float xv[4];
-          load4<T>(xb + (int64_t)tt * st + col, xv);
+    for (int j = 0; j < KS; ++j) {
+      const int tt = t - KS + 1 + j;
+      load16<T>(xb + (int64_t)max(tt, 0) * st, xv[j]);
+      if (tt < 0)
 #pragma unroll
-          for (int i = 0; i < 4; ++i) aw[j][i] += g[i] * xv[i];
-        }
-        // dx[t, d] += w[d, j] * dc[t + K - 1 - j, d]
-        const int tf = t + K - 1 - j;
-        if (tf < Tn) {
-          const float4 d4 = *reinterpret_cast<const float4*>(dc + (r + (K - 1 - j)) * D + col);
-          const float4 ww = *reinterpret_cast<const float4*>(wt + (int64_t)j * D + col);
-          o[0] += ww.x * d4.x; o[1] += ww.y * d4.y; o[2] += ww.z * d4.z; o[3] += ww.w * d4.w;
-        }
+        for (int i = 0; i < V; ++i) xv[j][i] = 0.f;
+    }
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      float a = bias ? bias[col + i] : 0.f;
+      if (wt) {
+#pragma unroll
+        for (int j = 0; j < KS; ++j) a += wt[(int64_t)j * D + col + i] * xv[j][i];
+      } else {
+        a += xv[KS - 1][i];
       }
-      store4<T>(dx + r * D + col, o);
+      o[i] = silu_(a);
+      ss += o[i] * o[i];
+    }
+  }
+  float inv = 1.f;
+  if (normalize) {
+    ss = warp_sum(ss);
+    if (lane == 0) red[threadIdx.y][wir] = ss;
+    __syncthreads();
+    float tot = 0.f;
+    for (int k = 0; k < (tpr >> 5); ++k) tot += red[threadIdx.y][k];
+    inv = 1.f / fmaxf(sqrtf(tot), kL2Eps);
+  }
+  if (active) {
+#pragma unroll
+    for (int i = 0; i < V; ++i) o[i] *= inv;
+    store16<T>(y + r * D + col, o);
+  }
+}
+
+// dc = d(loss)/d(conv output) (fp32, [rows, D]); without a conv it writes dx directly.
+template <typename T, int KS>
+__global__ void __launch_bounds__(512) conv_bwd_a_rows(const T* __restrict__ dy, const T* __restrict__ x,
+                                                       int64_t sb, int64_t st, const float* __restrict__ wt,
+                                                       const float* __restrict__ bias, float* __restrict__ dc,
+                                                       T* __restrict__ dx_direct, int64_t rows, int Tn, int D,
+                                                       bool normalize) {
+  constexpr int V = Vec16<T>::N;
+  __shared__ float red_s[32][33], red_d[32][33];
+  const int tpr = blockDim.x, lane = threadIdx.x & 31, wir = threadIdx.x >> 5;
+  const int64_t r = (int64_t)blockIdx.x * blockDim.y + threadIdx.y;
+  const int col = threadIdx.x * V;
+  const bool active = col < D && r < rows;
+  float pre[V], g[V];
+  float ss = 0.f, sd = 0.f;
+  if (active) {
+    const int b = (int)(r / Tn), t = (int)(r % Tn);
+    const T* xb = x + (int64_t)b * sb + col;
+    float xv[KS][V];
+#pragma unroll
+    for (int j = 0; j < KS; ++j) {
+      const int tt = t - KS + 1 + j;
+      load16<T>(xb + (int64_t)max(tt, 0) * st, xv[j]);
+      if (tt < 0)
+#pragma unroll
+        for (int i = 0; i < V; ++i) xv[j][i] = 0.f;
+    }
+    load16<T>(dy + r * D + col, g);
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      float a = bias ? bias[col + i] : 0.f;
+      if (wt) {
+#pragma unroll
+        for (int j = 0; j < KS; ++j) a += wt[(int64_t)j * D + col + i] * xv[j][i];
+      } else {
+        a += xv[KS - 1][i];
+      }
+      pre[i] = a;
+      const float s = silu_(a);
+      ss += s * s;
+      sd += s * g[i];
+    }
+  }
+  float den = 1.f, coef = 0.f;
+  if (normalize) {
+    ss = warp_sum(ss);
+    sd = warp_sum(sd);
+    if (lane == 0) { red_s[threadIdx.y][wir] = ss; red_d[threadIdx.y][wir] = sd; }
+    __syncthreads();
+    float ts = 0.f, td = 0.f;
+    for (int k = 0; k < (tpr >> 5); ++k) { ts += red_s[threadIdx.y][k]; td += red_d[threadIdx.y][k]; }
+    const float nrm = sqrtf(ts);
+    den = fmaxf(nrm, kL2Eps);
+    coef = nrm > kL2Eps ? td / (den * den) : 0.f;
+  }
+  if (active) {
+    float o[V];
+#pragma unroll
+    for (int i = 0; i < V; ++i) o[i] = (g[i] - silu_(pre[i]) * coef) / den * silu_grad_(pre[i]);
+    if (dc != nullptr) {
+#pragma unroll
+      for (int i = 0; i < V; i += 4)
+        *reinterpret_cast<float4*>(dc + r * D + col + i) = make_float4(o[i], o[i + 1], o[i + 2], o[i + 3]);
+    } else {
+      store16<T>(dx_direct + r * D + col, o);
+    }
+  }
+}
+
+// grid (splits, B, column groups): dx[t] = sum_j w[j] dc[t+KS-1-j];
+// dw[j] += dc[t] x[t-KS+1+j]; db += dc[t].  part: [splits*B][KS+1][D]
+template <typename T, int KS, int U>
+__global__ void __launch_bounds__(256) conv_bwd_b_rows(const float* __restrict__ dc, const T* __restrict__ x,
+                                                       int64_t sb, int64_t st, const float* __restrict__ wt,
+                                                       T* __restrict__ dx, float* __restrict__ part, int Tn, int D,
+                                                       int rows_per_split) {
+  constexpr int V = Vec16<T>::N;
+  constexpr int NR = U + KS - 1;
+  const int b = blockIdx.y, sp = blockIdx.x;
+  const int col = (blockIdx.z * blockDim.x + threadIdx.x) * V;
+  if (col >= D) return;
+  const int ts = sp * rows_per_split, te = min(Tn, ts + rows_per_split);
+  const T* xb = x + (int64_t)b * sb + col;
+  const float* dcb = dc + (int64_t)b * Tn * D + col;
+  float w[KS][V], aw[KS][V], ab[V];
+#pragma unroll
+  for (int j = 0; j < KS; ++j)
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      w[j][i] = wt[(int64_t)j * D + col + i];
+      aw[j][i] = 0.f;
+    }
+#pragma unroll
+  for (int i = 0; i < V; ++i) ab[i] = 0.f;
+  for (int t0 = ts; t0 < te; t0 += U) {
+    // rows needed: dc[t0 .. t0+U+KS-2] (zero past the end), x[t0-KS+1 .. t0+U-1] (zero before 0)
+    float dv[NR][V], xv[NR][V];
+#pragma unroll
+    for (int k = 0; k < NR; ++k) {
+      const int td = t0 + k;
+      const float* p = dcb + (int64_t)min(td, Tn - 1) * D;
+      const bool z = td >= Tn;
+#pragma unroll
+      for (int i = 0; i < V; i += 4) {
+        const float4 v = *reinterpret_cast<const float4*>(p + i);
+        dv[k][i] = z ? 0.f : v.x;
+        dv[k][i + 1] = z ? 0.f : v.y;
+        dv[k][i + 2] = z ? 0.f : v.z;
+        dv[k][i + 3] = z ? 0.f : v.w;
+      }
+      const int tx = t0 - KS + 1 + k;
+      load16<T>(xb + (int64_t)min(max(tx, 0), Tn - 1) * st, xv[k]);
+      if (tx < 0 || tx >= Tn)
+#pragma unroll
+        for (int i = 0; i < V; ++i) xv[k][i] = 0.f;
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int t = t0 + u;
+      if (t >= te) break;
+      float o[V];
+#pragma unroll
+      for (int i = 0; i < V; ++i) {
+        float a = 0.f;
+#pragma unroll
+        for (int j = 0; j < KS; ++j) {
+          a += w[j][i] * dv[u + KS - 1 - j][i];  // dc[t + KS - 1 - j]
+          aw[j][i] += dv[u][i] * xv[u + j][i];    // dc[t] * x[t - KS + 1 + j]
+        }
+        o[i] = a;
+        ab[i] += dv[u][i];
+      }
+      store16<T>(dx + ((int64_t)b * Tn + t) * D + col, o);
     }
   }
   if (part == nullptr) return;
+  float* pp = part + ((int64_t)(sp * gridDim.y + b)) * (KS + 1) * D + col;
 #pragma unroll
-  for (int j = 0; j < KMAX; ++j)
+  for (int j = 0; j < KS; ++j)
 #pragma unroll
-    for (int i = 0; i < 4; ++i) red[wid][j][lane * 4 + i] = aw[j][i];
+    for (int i = 0; i < V; ++i) pp[(int64_t)j * D + i] = aw[j][i];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) red[wid][KMAX][lane * 4 + i] = ab[i];
-  __syncthreads();
-  // part layout: [gridDim.y][K + 1][D]  (rows 0..K-1 = dw taps, row K = db)
-  for (int e = threadIdx.x; e < (K + 1) * 128; e += blockDim.x) {
-    const int j = e / 128, cc = e % 128;
-    const int gcol = blockIdx.x * 128 + cc;
-    if (gcol >= D) continue;
-    const int src = (j == K) ? KMAX : j;
-    float s = 0.f;
-#pragma unroll
-    for (int w = 0; w < 8; ++w) s += red[w][src][cc];
-    part[((int64_t)blockIdx.y * (K + 1) + j) * D + gcol] = s;
-  }
+  for (int i = 0; i < V; ++i) pp[(int64_t)KS * D + i] = ab[i];
 }
 
 __global__ void colsum_kernel2(const float* __restrict__ part, float* __restrict__ out, int G, int64_t N) {
@@ -247,47 +224,66 @@ __global__ void colsum_kernel2(const float* __restrict__ part, float* __restrict
   out[i] = s;
 }
 
-#define TB_CH4_SWITCH(CHN, ...)                              \
-  switch (CHN) {                                             \
-    case 1: { constexpr int CH = 1; __VA_ARGS__; break; }    \
-    case 2: { constexpr int CH = 2; __VA_ARGS__; break; }    \
-    case 3: { constexpr int CH = 3; __VA_ARGS__; break; }    \
-    case 4: { constexpr int CH = 4; __VA_ARGS__; break; }    \
-    case 5: case 6: { constexpr int CH = 6; __VA_ARGS__; break; } \
-    case 7: case 8: { constexpr int CH = 8; __VA_ARGS__; break; } \
-    case 9: case 10: case 11: case 12: { constexpr int CH = 12; __VA_ARGS__; break; } \
-    default: { constexpr int CH = 16; __VA_ARGS__; break; }  \
+#define TB_KS_SWITCH(KV, ...)                                  \
+  switch (KV) {                                                \
+    case 1: { constexpr int KS = 1; __VA_ARGS__; break; }      \
+    case 2: { constexpr int KS = 2; __VA_ARGS__; break; }      \
+    case 3: { constexpr int KS = 3; __VA_ARGS__; break; }      \
+    case 4: { constexpr int KS = 4; __VA_ARGS__; break; }      \
+    case 5: { constexpr int KS = 5; __VA_ARGS__; break; }      \
+    case 6: { constexpr int KS = 6; __VA_ARGS__; break; }      \
+    case 7: { constexpr int KS = 7; __VA_ARGS__; break; }      \
+    case 8: { constexpr int KS = 8; __VA_ARGS__; break; }      \
+    default: TORCH_CHECK(false, "conv kernel size must be 1..8"); \
   }
+
+#define TB_DISPATCH_BF16_F32(dtype, NAME, ...)                  \
+  [&] {                                                         \
+    if ((dtype) == at::kBFloat16) {                             \
+      using scalar_t = __nv_bfloat16;                           \
+      return __VA_ARGS__();                                     \
+    } else if ((dtype) == at::kFloat) {                         \
+      using scalar_t = float;                                   \
+      return __VA_ARGS__();                                     \
+    }                                                           \
+    TORCH_CHECK(false, NAME, ": bf16 or fp32 only, got ", dtype); \
+  }()
 
 static at::Tensor conv_wt(const c10::optional<at::Tensor>& w, int D) {
   if (!w.has_value() || !w->defined()) return at::Tensor();
-  // [D, 1, K] -> [K, D] fp32
-  return w->reshape({D, -1}).t().contiguous().to(at::kFloat);
+  return w->reshape({D, -1}).t().contiguous().to(at::kFloat);  // [D,1,K] -> [K, D] fp32
 }
+
+static void check_x(const at::Tensor& x, int V) {
+  TORCH_CHECK(x.dim() == 3 && x.stride(2) == 1, "conv_silu_norm: x must be [B, T, D] with a contiguous last dim");
+  const int D = x.size(2);
+  TORCH_CHECK(D % V == 0 && x.stride(1) % V == 0 && x.stride(0) % V == 0 && aligned16(x),
+              "conv_silu_norm: D, row strides and base must be 16-byte multiples");
+  TORCH_CHECK(D / V <= 512, "conv_silu_norm: D too large (at most 512 16-byte slices per row)");
+}
+
+static int threads_for(int D, int V) { return ((D / V) + 31) / 32 * 32; }
+static dim3 row_block(int tpr) { return dim3(tpr, std::max(1, std::min(32, 512 / tpr))); }
 
 at::Tensor conv_silu_norm_fwd(const at::Tensor& x, const c10::optional<at::Tensor>& w,
                               const c10::optional<at::Tensor>& b, bool normalize) {
   TB_CHECK_CUDA(x);
-  TB_CHECK_LASTDIM(x);
-  TORCH_CHECK(x.dim() == 3, "conv_silu_norm: x must be [B, T, D]");
   const at::cuda::CUDAGuard g(x.device());
   const int B = x.size(0), Tn = x.size(1), D = x.size(2);
-  TORCH_CHECK(D % 4 == 0 && x.stride(1) % 4 == 0 && x.stride(0) % 4 == 0, "conv_silu_norm: D and strides must be multiples of 4");
-  TORCH_CHECK(((uintptr_t)x.data_ptr() % (4 * x.element_size())) == 0, "conv_silu_norm: x must be aligned to 4 elements");
   at::Tensor wt = conv_wt(w, D);
-  const int K = wt.defined() ? wt.size(0) : 0;
-  TORCH_CHECK(K <= 8, "conv kernel size must be <= 8");
+  const int K = wt.defined() ? wt.size(0) : 1;
   at::Tensor bias = (b.has_value() && b->defined()) ? b->to(at::kFloat).contiguous() : at::Tensor();
   at::Tensor y = at::empty({B, Tn, D}, x.options());
   const int64_t rows = (int64_t)B * Tn;
   if (rows == 0) return y;
-  const int chn = (D + 127) / 128;
-  TORCH_CHECK(chn <= 16, "conv_silu_norm: D too large");
-  const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>((rows + 7) / 8, (int64_t)num_sms() * 8));
-  TB_DISPATCH_FLOAT(x.scalar_type(), "conv_silu_norm_fwd", [&] {
-    TB_CH4_SWITCH(chn, conv_fwd_kernel<scalar_t, CH><<<blocks, 256, 0, stream()>>>(
+  TB_DISPATCH_BF16_F32(x.scalar_type(), "conv_silu_norm_fwd", [&] {
+    constexpr int V = Vec16<scalar_t>::N;
+    check_x(x, V);
+    const dim3 blk = row_block(threads_for(D, V));
+    const int64_t grid = (rows + blk.y - 1) / blk.y;
+    TB_KS_SWITCH(K, conv_fwd_rows<scalar_t, KS><<<grid, blk, 0, stream()>>>(
         (const scalar_t*)x.data_ptr(), x.stride(0), x.stride(1), wt.defined() ? wt.data_ptr<float>() : nullptr,
-        bias.defined() ? bias.data_ptr<float>() : nullptr, (scalar_t*)y.data_ptr(), B, Tn, D, K, normalize));
+        bias.defined() ? bias.data_ptr<float>() : nullptr, (scalar_t*)y.data_ptr(), rows, Tn, D, normalize));
   });
   check_launch("conv_silu_norm_fwd");
   return y;
@@ -299,37 +295,44 @@ std::vector<at::Tensor> conv_silu_norm_bwd(const at::Tensor& dy, const at::Tenso
   TB_CHECK_CUDA(x);
   const at::cuda::CUDAGuard g(x.device());
   const int B = x.size(0), Tn = x.size(1), D = x.size(2);
-  at::Tensor dyc = contig16(dy);
-  TORCH_CHECK(x.stride(2) == 1 && x.stride(1) % 4 == 0 && x.stride(0) % 4 == 0 && D % 4 == 0 &&
-              ((uintptr_t)x.data_ptr() % (4 * x.element_size())) == 0, "conv_silu_norm_bwd: x layout");
+  at::Tensor dyc = contig16(dy.to(x.scalar_type()));
   at::Tensor wt = conv_wt(w, D);
-  const int K = wt.defined() ? wt.size(0) : 0;
+  const int K = wt.defined() ? wt.size(0) : 1;
   at::Tensor bias = (b.has_value() && b->defined()) ? b->to(at::kFloat).contiguous() : at::Tensor();
   at::Tensor dx = at::empty({B, Tn, D}, x.options());
   at::Tensor dw = at::empty({0}, x.options().dtype(at::kFloat)), db = at::empty({0}, x.options().dtype(at::kFloat));
   const int64_t rows = (int64_t)B * Tn;
   if (rows == 0) return {dx.zero_(), dw, db};
-  const int chn = (D + 127) / 128;
-  const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>((rows + 7) / 8, (int64_t)num_sms() * 8));
   at::Tensor dc = wt.defined() ? at::empty({B, Tn, D}, x.options().dtype(at::kFloat)) : at::Tensor();
-  TB_DISPATCH_FLOAT(x.scalar_type(), "conv_silu_norm_bwd", [&] {
-    TB_CH4_SWITCH(chn, conv_bwd_a_kernel<scalar_t, CH><<<blocks, 256, 0, stream()>>>(
+  TB_DISPATCH_BF16_F32(x.scalar_type(), "conv_silu_norm_bwd", [&] {
+    constexpr int V = Vec16<scalar_t>::N;
+    check_x(x, V);
+    const int tpr = threads_for(D, V);
+    const dim3 blk = row_block(tpr);
+    const int64_t grid = (rows + blk.y - 1) / blk.y;
+    TB_KS_SWITCH(K, conv_bwd_a_rows<scalar_t, KS><<<grid, blk, 0, stream()>>>(
         (const scalar_t*)dyc.data_ptr(), (const scalar_t*)x.data_ptr(), x.stride(0), x.stride(1),
         wt.defined() ? wt.data_ptr<float>() : nullptr, bias.defined() ? bias.data_ptr<float>() : nullptr,
-        dc.defined() ? dc.data_ptr<float>() : nullptr, (scalar_t*)dx.data_ptr(), B, Tn, D, K, normalize));
+        dc.defined() ? dc.data_ptr<float>() : nullptr, (scalar_t*)dx.data_ptr(), rows, Tn, D, normalize));
     check_launch("conv_silu_norm_bwd_a");
     if (wt.defined()) {
-      const int gy = (int)std::max<int64_t>(1, std::min<int64_t>((rows + 7) / 8, (int64_t)num_sms() * 4 / ((D + 127) / 128) + 1));
-      at::Tensor part = need_wgrad ? at::empty({gy, K + 1, D}, x.options().dtype(at::kFloat)) : at::Tensor();
-      dim3 grid((D + 127) / 128, gy);
-      conv_bwd_b_kernel<scalar_t><<<grid, 256, 0, stream()>>>(
+      const int want_warps = num_sms() * 24;
+      int splits = std::max(1, want_warps / std::max(1, B * (tpr / 32)));
+      splits = std::min(splits, std::max(1, Tn / 8));
+      const int rps = (Tn + splits - 1) / splits;
+      splits = (Tn + rps - 1) / rps;
+      at::Tensor part = need_wgrad ? at::empty({splits * B, K + 1, D}, x.options().dtype(at::kFloat)) : at::Tensor();
+      const int bx = std::min(tpr, 256);
+      dim3 g2(splits, B, (tpr + bx - 1) / bx);
+      TB_KS_SWITCH(K, conv_bwd_b_rows<scalar_t, KS, 2><<<g2, bx, 0, stream()>>>(
           dc.data_ptr<float>(), (const scalar_t*)x.data_ptr(), x.stride(0), x.stride(1), wt.data_ptr<float>(),
-          (scalar_t*)dx.data_ptr(), need_wgrad ? part.data_ptr<float>() : nullptr, B, Tn, D, K);
+          (scalar_t*)dx.data_ptr(), need_wgrad ? part.data_ptr<float>() : nullptr, Tn, D, rps));
       check_launch("conv_silu_norm_bwd_b");
       if (need_wgrad) {
         at::Tensor red = at::empty({K + 1, D}, x.options().dtype(at::kFloat));
         const int64_t N = (int64_t)(K + 1) * D;
-        colsum_kernel2<<<(N + 255) / 256, 256, 0, stream()>>>(part.data_ptr<float>(), red.data_ptr<float>(), gy, N);
+        colsum_kernel2<<<(N + 255) / 256, 256, 0, stream()>>>(part.data_ptr<float>(), red.data_ptr<float>(),
+                                                              splits * B, N);
         check_launch("conv_silu_norm_bwd colsum");
         dw = red.narrow(0, 0, K).t().contiguous();  // [D, K]
         db = red[K].contiguous();

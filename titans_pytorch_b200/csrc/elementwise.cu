@@ -157,23 +157,29 @@ __global__ void seq_sum_kernel(const T* __restrict__ x, int64_t sb, int64_t st, 
   part[((int64_t)s * B + b) * D + d] = acc;
 }
 
-// one block per (gate, 32 output features); warp per output feature.
-// part_out[(gate * nblk_per_gate + blk)] = sum over (b, o in blk) sigmoid(z)
+// xm[b, d] = mean over the sequence (sum of the split partials), rounded to the
+// input dtype as x.mean() in that dtype does.  Done once, not per GEMV block.
 template <typename T>
-__global__ void gate_gemv_kernel(const float* __restrict__ part, int splits, const T* __restrict__ W0,
-                                 const T* __restrict__ W1, const T* __restrict__ W2, const T* __restrict__ b0,
-                                 const T* __restrict__ b1, const T* __restrict__ b2, float* __restrict__ sig_part,
-                                 int B, int Tn, int D) {
+__global__ void seq_mean_finish_kernel(const float* __restrict__ part, int splits, float* __restrict__ xm, int BD,
+                                       int Tn) {
+  const int e = blockIdx.x * blockDim.x + threadIdx.x;
+  if (e >= BD) return;
+  float s = 0.f;
+  for (int k = 0; k < splits; ++k) s += part[(int64_t)k * BD + e];
+  xm[e] = to_f<T>(from_f<T>(s / (float)Tn));
+}
+
+// grid (nblk, 3 gates); warp per output feature.
+// sig_part[gate, blk] = sum over (b, o in blk) sigmoid(z)
+template <typename T>
+__global__ void gate_gemv_kernel(const float* __restrict__ xm_g, const T* __restrict__ W0, const T* __restrict__ W1,
+                                 const T* __restrict__ W2, const T* __restrict__ b0, const T* __restrict__ b1,
+                                 const T* __restrict__ b2, float* __restrict__ sig_part, int B, int D) {
   extern __shared__ float xm[];  // [B, D] sequence means
   const int gate = blockIdx.y;
   const T* W = gate == 0 ? W0 : (gate == 1 ? W1 : W2);
   const T* bb = gate == 0 ? b0 : (gate == 1 ? b1 : b2);
-  for (int e = threadIdx.x; e < B * D; e += blockDim.x) {
-    float s = 0.f;
-    for (int k = 0; k < splits; ++k) s += part[(int64_t)k * B * D + e];
-    // round the mean to the input dtype, as x.mean() does in that dtype
-    xm[e] = to_f<T>(from_f<T>(s / (float)Tn));
-  }
+  for (int e = threadIdx.x; e < B * D; e += blockDim.x) xm[e] = xm_g[e];
   __syncthreads();
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
   float local = 0.f;
@@ -184,7 +190,8 @@ __global__ void gate_gemv_kernel(const float* __restrict__ part, int splits, con
       float acc = 0.f;
       for (int d = lane; d < D; d += 32) acc += xm[b * D + d] * to_f<T>(wr[d]);
       acc = warp_sum(acc) + bias;
-      if (lane == 0) local += sigmoidf_(acc);
+      // round the logit to the input dtype, as the reference's Linear output is
+      if (lane == 0) local += sigmoidf_(to_f<T>(from_f<T>(acc)));
     }
   }
   __shared__ float red[32];
@@ -233,12 +240,15 @@ at::Tensor memory_gates(const at::Tensor& x, const std::vector<at::Tensor>& ws, 
     TORCH_CHECK(smem <= 200 * 1024, "memory_gates: B*D too large for one block's shared memory");
     if (smem > 48 * 1024)
       cudaFuncSetAttribute(gate_gemv_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    at::Tensor xm = at::empty({B, D}, x.options().dtype(at::kFloat));
+    seq_mean_finish_kernel<T><<<(B * D + 255) / 256, 256, 0, stream()>>>(part.data_ptr<float>(), splits,
+                                                                        xm.data_ptr<float>(), B * D, Tn);
     dim3 g2(nblk, 3);
     gate_gemv_kernel<T><<<g2, 256, smem, stream()>>>(
-        part.data_ptr<float>(), splits, (const T*)wc[0].data_ptr(), (const T*)wc[1].data_ptr(),
+        xm.data_ptr<float>(), (const T*)wc[0].data_ptr(), (const T*)wc[1].data_ptr(),
         (const T*)wc[2].data_ptr(), bc[0].defined() ? (const T*)bc[0].data_ptr() : nullptr,
         bc[1].defined() ? (const T*)bc[1].data_ptr() : nullptr, bc[2].defined() ? (const T*)bc[2].data_ptr() : nullptr,
-        sig.data_ptr<float>(), B, Tn, D);
+        sig.data_ptr<float>(), B, D);
     gate_finish_kernel<<<1, 32, 0, stream()>>>(sig.data_ptr<float>(), nblk, B, D, (float)lr, (float)mom,
                                                gates.data_ptr<float>());
   });

@@ -219,19 +219,26 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       const int pre_hi = min(BN, max(0, P - n0));
       const int lo2 = max(pre_hi, P - n0 + win_lo);
       const int hi2 = min(BN, P - n0 + win_hi + 1);
+      const bool row_full = (pre_hi >= BN) || (lo2 <= pre_hi && pre_hi == 0 && lo2 <= 0 && hi2 >= BN);
       float mx[8];
 #pragma unroll
       for (int k = 0; k < 8; ++k) mx[k] = -INFINITY;
+      if (__all_sync(0xffffffffu, row_full)) {
+        // every row of this warp sees the whole tile: no masking
 #pragma unroll
-      for (int c = 0; c < BN; ++c) {
-        const bool vis = (c < pre_hi) || (c >= lo2 && c < hi2);
-        const float v = vis ? s[c] * scale_log2 : -INFINITY;
-        s[c] = v;
-        mx[c & 7] = fmaxf(mx[c & 7], v);
+        for (int c = 0; c < BN; ++c) mx[c & 7] = fmaxf(mx[c & 7], s[c]);
+      } else {
+#pragma unroll
+        for (int c = 0; c < BN; ++c) {
+          const bool vis = (c < pre_hi) | ((c >= lo2) & (c < hi2));
+          s[c] = vis ? s[c] : -INFINITY;
+          mx[c & 7] = fmaxf(mx[c & 7], s[c]);
+        }
       }
-      const float mxa = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
-                              fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
-      const float m_new = fmaxf(m_run, mxa);
+      // raw-score max; the softmax scale (> 0) is folded into one FFMA before ex2
+      const float mraw = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                               fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+      const float m_new = fmaxf(m_run, mraw * scale_log2);
       const float m_use = m_new == -INFINITY ? 0.f : m_new;
       const float corr = ex2(m_run - m_use);
       float sm[8];
@@ -240,7 +247,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       uint32_t pk[BN / 2];
 #pragma unroll
       for (int c = 0; c < BN; c += 2) {
-        const float p0 = ex2(s[c] - m_use), p1 = ex2(s[c + 1] - m_use);
+        const float p0 = ex2(fmaf(s[c], scale_log2, -m_use)), p1 = ex2(fmaf(s[c + 1], scale_log2, -m_use));
         sm[(c >> 1) & 7] += p0 + p1;
         pk[c / 2] = pack2(p0, p1);
       }

@@ -18,6 +18,21 @@ namespace tb {
 
 constexpr float kL2Eps = 1e-12f;  // F.normalize default eps
 
+// N consecutive fp32 values starting at column col (N a multiple of 4, col
+// 4-aligned) with float4 loads; zeros when p is null.
+template <int N>
+__device__ __forceinline__ void load_cols_f32(const float* __restrict__ p, int col, float (&o)[N]) {
+#pragma unroll
+  for (int i = 0; i < N; i += 4) {
+    if (p) {
+      const float4 v = *reinterpret_cast<const float4*>(p + col + i);
+      o[i] = v.x; o[i + 1] = v.y; o[i + 2] = v.z; o[i + 3] = v.w;
+    } else {
+      o[i] = o[i + 1] = o[i + 2] = o[i + 3] = 0.f;
+    }
+  }
+}
+
 template <typename T, int KS>
 __global__ void __launch_bounds__(512) conv_fwd_rows(const T* __restrict__ x, int64_t sb, int64_t st,
                                                      const float* __restrict__ wt, const float* __restrict__ bias,
@@ -42,16 +57,23 @@ __global__ void __launch_bounds__(512) conv_fwd_rows(const T* __restrict__ x, in
 #pragma unroll
         for (int i = 0; i < V; ++i) xv[j][i] = 0.f;
     }
+    float acc[V];
+    load_cols_f32(bias, col, acc);
+    if (wt) {
+#pragma unroll
+      for (int j = 0; j < KS; ++j) {
+        float wj[V];
+        load_cols_f32(wt + (int64_t)j * D, col, wj);
+#pragma unroll
+        for (int i = 0; i < V; ++i) acc[i] += wj[i] * xv[j][i];
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < V; ++i) acc[i] += xv[KS - 1][i];
+    }
 #pragma unroll
     for (int i = 0; i < V; ++i) {
-      float a = bias ? bias[col + i] : 0.f;
-      if (wt) {
-#pragma unroll
-        for (int j = 0; j < KS; ++j) a += wt[(int64_t)j * D + col + i] * xv[j][i];
-      } else {
-        a += xv[KS - 1][i];
-      }
-      o[i] = silu_(a);
+      o[i] = silu_(acc[i]);
       ss += o[i] * o[i];
     }
   }
@@ -99,17 +121,22 @@ __global__ void __launch_bounds__(512) conv_bwd_a_rows(const T* __restrict__ dy,
         for (int i = 0; i < V; ++i) xv[j][i] = 0.f;
     }
     load16<T>(dy + r * D + col, g);
+    load_cols_f32(bias, col, pre);
+    if (wt) {
+#pragma unroll
+      for (int j = 0; j < KS; ++j) {
+        float wj[V];
+        load_cols_f32(wt + (int64_t)j * D, col, wj);
+#pragma unroll
+        for (int i = 0; i < V; ++i) pre[i] += wj[i] * xv[j][i];
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < V; ++i) pre[i] += xv[KS - 1][i];
+    }
 #pragma unroll
     for (int i = 0; i < V; ++i) {
-      float a = bias ? bias[col + i] : 0.f;
-      if (wt) {
-#pragma unroll
-        for (int j = 0; j < KS; ++j) a += wt[(int64_t)j * D + col + i] * xv[j][i];
-      } else {
-        a += xv[KS - 1][i];
-      }
-      pre[i] = a;
-      const float s = silu_(a);
+      const float s = silu_(pre[i]);
       ss += s * s;
       sd += s * g[i];
     }
@@ -157,12 +184,11 @@ __global__ void __launch_bounds__(256) conv_bwd_b_rows(const float* __restrict__
   const float* dcb = dc + (int64_t)b * Tn * D + col;
   float w[KS][V], aw[KS][V], ab[V];
 #pragma unroll
-  for (int j = 0; j < KS; ++j)
+  for (int j = 0; j < KS; ++j) {
+    load_cols_f32(wt + (int64_t)j * D, col, w[j]);
 #pragma unroll
-    for (int i = 0; i < V; ++i) {
-      w[j][i] = wt[(int64_t)j * D + col + i];
-      aw[j][i] = 0.f;
-    }
+    for (int i = 0; i < V; ++i) aw[j][i] = 0.f;
+  }
 #pragma unroll
   for (int i = 0; i < V; ++i) ab[i] = 0.f;
   for (int t0 = ts; t0 < te; t0 += U) {
@@ -216,12 +242,23 @@ __global__ void __launch_bounds__(256) conv_bwd_b_rows(const float* __restrict__
   for (int i = 0; i < V; ++i) pp[(int64_t)KS * D + i] = ab[i];
 }
 
+// out[i] = sum_g part[g, i]: block (32 columns x 8 row groups); each thread
+// sums every 8th row of its column, then the 8 partials are added in a fixed
+// order (deterministic).
 __global__ void colsum_kernel2(const float* __restrict__ part, float* __restrict__ out, int G, int64_t N) {
-  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= N) return;
+  __shared__ float red[8][33];
+  const int64_t i = (int64_t)blockIdx.x * 32 + threadIdx.x;
   float s = 0.f;
-  for (int g = 0; g < G; ++g) s += part[(int64_t)g * N + i];
-  out[i] = s;
+  if (i < N)
+    for (int g = threadIdx.y; g < G; g += 8) s += part[(int64_t)g * N + i];
+  red[threadIdx.y][threadIdx.x] = s;
+  __syncthreads();
+  if (threadIdx.y == 0 && i < N) {
+    float t = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) t += red[k][threadIdx.x];
+    out[i] = t;
+  }
 }
 
 #define TB_KS_SWITCH(KV, ...)                                  \
@@ -263,7 +300,7 @@ static void check_x(const at::Tensor& x, int V) {
 }
 
 static int threads_for(int D, int V) { return ((D / V) + 31) / 32 * 32; }
-static dim3 row_block(int tpr) { return dim3(tpr, std::max(1, std::min(32, 512 / tpr))); }
+static dim3 row_block(int tpr) { return dim3(tpr, std::max(1, std::min(32, 256 / tpr))); }
 
 at::Tensor conv_silu_norm_fwd(const at::Tensor& x, const c10::optional<at::Tensor>& w,
                               const c10::optional<at::Tensor>& b, bool normalize) {
@@ -316,7 +353,7 @@ std::vector<at::Tensor> conv_silu_norm_bwd(const at::Tensor& dy, const at::Tenso
         dc.defined() ? dc.data_ptr<float>() : nullptr, (scalar_t*)dx.data_ptr(), rows, Tn, D, normalize));
     check_launch("conv_silu_norm_bwd_a");
     if (wt.defined()) {
-      const int want_warps = num_sms() * 24;
+      const int want_warps = num_sms() * 12;
       int splits = std::max(1, want_warps / std::max(1, B * (tpr / 32)));
       splits = std::min(splits, std::max(1, Tn / 8));
       const int rps = (Tn + splits - 1) / splits;
@@ -331,8 +368,8 @@ std::vector<at::Tensor> conv_silu_norm_bwd(const at::Tensor& dy, const at::Tenso
       if (need_wgrad) {
         at::Tensor red = at::empty({K + 1, D}, x.options().dtype(at::kFloat));
         const int64_t N = (int64_t)(K + 1) * D;
-        colsum_kernel2<<<(N + 255) / 256, 256, 0, stream()>>>(part.data_ptr<float>(), red.data_ptr<float>(),
-                                                              splits * B, N);
+        colsum_kernel2<<<(N + 31) / 32, dim3(32, 8), 0, stream()>>>(part.data_ptr<float>(), red.data_ptr<float>(),
+                                                                    splits * B, N);
         check_launch("conv_silu_norm_bwd colsum");
         dw = red.narrow(0, 0, K).t().contiguous();  // [D, K]
         db = red[K].contiguous();

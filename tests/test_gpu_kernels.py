@@ -229,3 +229,24 @@ def test_attention_tcgen05_forward(case):
     assert rel_err(o_tc, ref) < 1e-2
     assert rel_err(o_tc, o_mma) < 1e-2
     assert float((l_tc - lse_ref).abs().max()) < 2e-2
+
+
+@pytest.mark.parametrize("case", TC_CASES + [(1, 2, 1100, 4, 512), (2, 1, 700, 16, 100)])
+def test_attention_tcgen05_backward(case):
+    """tcgen05 backward vs the mma.sync backward (both against the same forward outputs)."""
+    B, H, T, P, W = case
+    E = _ext.ext()
+    torch.manual_seed(8)
+    d = 64
+    Q = torch.randn(B, H, T, d, device=DEV, dtype=torch.bfloat16)
+    K = torch.randn(B, H, P + T, d, device=DEV, dtype=torch.bfloat16)
+    V = torch.randn(B, H, P + T, d, device=DEV, dtype=torch.bfloat16)
+    scale = d ** -0.5
+    O, lse = E.attn_fwd_tc(Q, K, V, W, scale)
+    dO = torch.randn_like(O)
+    a = E.attn_bwd_tc(dO, Q, K, V, O, lse, W, scale)
+    r = E.attn_bwd_packed(dO, Q, K, V, O, lse, W, scale)
+    torch.cuda.synchronize()
+    assert E.kernel_error_status(0, True) == 0
+    for x, y in zip(a, r):
+        assert rel_err(x, y) < 1e-2

@@ -406,3 +406,401 @@ std::vector<at::Tensor> attn_fwd_tc(const at::Tensor& Q, const at::Tensor& K, co
 }
 
 }  // namespace tb
+
+namespace tb {
+
+// =============================================================================
+// Backward, head_dim 64, on tcgen05.
+//
+// One CTA = one (batch, head), one tile of 128 keys (the M dimension of the
+// key-major products) and a range of 128-query blocks (the queries that can see
+// those keys; the prefix tile, seen by every query, is split across CTAs).
+// 6 warps: warp 4 TMA producer (K, V once; Q, dO, log-sum-exp and D per query
+// block through a 2-stage ring), warp 5 TMEM allocator + MMA issuer, warps 0..3
+// one thread per key row (= TMEM lane).  Per query block:
+//   S^T  = K Q^T      (M=128 keys, N=128 queries, K=64)      -> TMEM
+//   dP^T = V dO^T     (M=128, N=128, K=64)                    -> TMEM
+//   threads: P^T = exp2(S^T*scale*log2e - lse2), dS^T = P^T (dP^T - D), both
+//            written as bf16 into shared memory in the UMMA K-major layout
+//   dV  += P^T dO     (M=128 keys, N=64, K=128; dO as an MN-major operand)
+//   dK  += dS^T Q     (same shapes; Q as an MN-major operand)
+//   dQ   = dS K       (M=128 queries, N=64, K=128 keys; dS read as an MN-major
+//                      operand straight from the dS^T tile, K as MN-major)
+//   threads: dQ rows (TMEM lanes = queries) -> red.global.add.v4.f32 into dQa
+// At the end dK (scaled) and dV rows go to dKa / dVa with vector reductions
+// (a key tile can be shared by several CTAs).  All waits are bounded.
+// =============================================================================
+namespace attn_tcb {
+
+using bf16 = __nv_bfloat16;
+constexpr int HD = 64, BN = 128, BQ = 128;
+constexpr int TILE = 128 * 64 * 2;  // 16 KB: one [128 rows][64 bf16] swizzled tile
+constexpr int OFF_K = 0, OFF_V = OFF_K + TILE, OFF_Q = OFF_V + TILE, OFF_DO = OFF_Q + 2 * TILE;
+constexpr int OFF_PT = OFF_DO + 2 * TILE, OFF_DST = OFF_PT + 2 * TILE;
+constexpr int OFF_L = OFF_DST + 2 * TILE, OFF_D = OFF_L + 2 * BQ * 4, OFF_BAR = OFF_D + 2 * BQ * 4;
+constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;
+constexpr uint32_t TM_ST = 0, TM_DPT = 128, TM_DV = 256, TM_DK = 320, TM_DQ = 384, TM_COLS = 512;
+constexpr int QB_PER_SPLIT = 6;
+
+__device__ __forceinline__ uint32_t pack2(float a, float b) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;\n" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// D[bh, i] = sum_d dO * O, lse2 = LSE * log2(e); both [BH][Tpad], zero padded.
+__global__ void bwd_pre_tc_kernel(const bf16* __restrict__ dO, const bf16* __restrict__ O,
+                                  const float* __restrict__ LSE, float* __restrict__ Dd, float* __restrict__ L2,
+                                  int B, int H, int Tn, int Tpad) {
+  const int64_t rows = (int64_t)B * H * Tpad;
+  const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;  // 8 threads per row
+  const int64_t r = e >> 3;
+  const int c = (int)(e & 7);
+  float acc = 0.f;
+  const int i = (int)(r % Tpad);
+  const int64_t bh = r / Tpad;
+  if (r < rows && i < Tn) {
+    const int b = (int)(bh / H), h = (int)(bh % H);
+    const int64_t off = (((int64_t)b * Tn + i) * H + h) * HD + c * 8;
+    float a[8], o[8];
+    load16<bf16>(dO + off, a);
+    load16<bf16>(O + off, o);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) acc += a[k] * o[k];
+  }
+  acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+  acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+  acc += __shfl_xor_sync(0xffffffffu, acc, 4);
+  if (r < rows && c == 0) {
+    Dd[r] = acc;
+    L2[r] = i < Tn ? LSE[bh * Tn + i] * 1.4426950408889634f : 0.f;
+  }
+}
+
+__global__ void __launch_bounds__(192, 1)
+    attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+                       const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmDO,
+                       const float* __restrict__ L2, const float* __restrict__ Dd, float* __restrict__ dQa,
+                       float* __restrict__ dKa, float* __restrict__ dVa, int H, int Tn, int Tpad, int P, int W,
+                       float scale, float scale_log2, int splits, unsigned* __restrict__ err) {
+  const int bh = blockIdx.y;
+  const int kt = blockIdx.x / splits, sp = blockIdx.x % splits;
+  const int n0 = kt * BN;
+  const int L = P + Tn;
+  if (n0 >= L) return;
+  // query range that can see this key tile
+  int q_lo, q_hi;
+  if (n0 < P) {
+    q_lo = 0;
+    q_hi = Tn - 1;
+  } else {
+    q_lo = n0 - P;
+    q_hi = min(Tn - 1, min(n0 + BN, L) - 1 - P + W - 1);
+  }
+  const int qb_lo = q_lo / BQ, qb_hi = q_hi / BQ;
+  const int nqb = qb_hi - qb_lo + 1;
+  const int nsp = min(splits, (nqb + QB_PER_SPLIT - 1) / QB_PER_SPLIT);
+  if (sp >= nsp) return;
+  const int per = (nqb + nsp - 1) / nsp;
+  const int qs = qb_lo + sp * per, qe = min(qb_hi + 1, qs + per);
+  const int nq = qe - qs;
+  if (nq <= 0) return;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
+  uint64_t* bar_kv = bars + 0;
+  uint64_t* bar_q_full = bars + 1;   // [2]
+  uint64_t* bar_q_empty = bars + 3;  // [2]
+  uint64_t* bar_s_full = bars + 5;
+  uint64_t* bar_p_full = bars + 6;
+  uint64_t* bar_mma_done = bars + 7;
+  uint64_t* bar_dq_free = bars + 8;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int b = bh / H, h = bh % H;
+
+  if (threadIdx.x == 0) {
+    tc::mbar_init(bar_kv, 1);
+    for (int s = 0; s < 2; ++s) {
+      tc::mbar_init(bar_q_full + s, 1);
+      tc::mbar_init(bar_q_empty + s, 1);
+    }
+    tc::mbar_init(bar_s_full, 1);
+    tc::mbar_init(bar_p_full, 128);
+    tc::mbar_init(bar_mma_done, 1);
+    tc::mbar_init(bar_dq_free, 128);
+    *abort_flag = 0;
+    tc::mbar_fence_init();
+  }
+  if (warp == 5) {
+    tc::tmem_alloc(tmem_slot, TM_COLS);
+    tc::tmem_relinquish();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 4) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      tc::mbar_expect_tx(bar_kv, 2 * TILE);
+      tc::tma_load_3d(smem + OFF_K, &tmK, bar_kv, 0, n0, bh);
+      tc::tma_load_3d(smem + OFF_V, &tmV, bar_kv, 0, n0, bh);
+      int issued = 0;
+      for (int j = 0; j < nq; ++j) {
+        const int s = j & 1;
+        if (j >= 2 && !tc::mbar_wait(bar_q_empty + s, ((j >> 1) - 1) & 1, abort_flag, err)) break;
+        const int q0 = (qs + j) * BQ;
+        tc::mbar_expect_tx(bar_q_full + s, 2 * TILE + 2 * BQ * 4);
+        tc::tma_load_3d(smem + OFF_Q + s * TILE, &tmQ, bar_q_full + s, 0, q0, bh);
+        tc::tma_load_4d(smem + OFF_DO + s * TILE, &tmDO, bar_q_full + s, 0, h, q0, b);
+        tc::bulk_load(smem + OFF_L + s * BQ * 4, L2 + (int64_t)bh * Tpad + q0, BQ * 4, bar_q_full + s);
+        tc::bulk_load(smem + OFF_D + s * BQ * 4, Dd + (int64_t)bh * Tpad + q0, BQ * 4, bar_q_full + s);
+        issued = j + 1;
+      }
+      if (*abort_flag) {
+        volatile int keep_waiting = 0;
+        tc::mbar_wait(bar_kv, 0, &keep_waiting, nullptr, 1ll << 27);
+        for (int j = max(0, issued - 2); j < issued; ++j)
+          tc::mbar_wait(bar_q_full + (j & 1), (j >> 1) & 1, &keep_waiting, nullptr, 1ll << 27);
+      }
+    }
+  } else if (warp == 5) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t id_s = tc::idesc_bf16_f32(128, 128, false, false);
+      constexpr uint32_t id_kv = tc::idesc_bf16_f32(128, HD, false, true);  // dV, dK: B (dO / Q) MN-major
+      constexpr uint32_t id_q = tc::idesc_bf16_f32(128, HD, true, true);    // dQ: A (dS) and B (K) MN-major
+      const uint32_t aK = tc::smem_addr(smem + OFF_K), aV = tc::smem_addr(smem + OFF_V);
+      const uint32_t aPT = tc::smem_addr(smem + OFF_PT), aDST = tc::smem_addr(smem + OFF_DST);
+      bool ok = tc::mbar_wait(bar_kv, 0, abort_flag, err);
+      auto issue_sdp = [&](int j) -> bool {
+        const int s = j & 1;
+        if (!tc::mbar_wait(bar_q_full + s, (j >> 1) & 1, abort_flag, err)) return false;
+        tc::tc_fence_after();
+        const uint32_t aQ = tc::smem_addr(smem + OFF_Q + s * TILE), aDO = tc::smem_addr(smem + OFF_DO + s * TILE);
+#pragma unroll
+        for (int k = 0; k < HD / 16; ++k)
+          tc::umma_bf16(tmem + TM_ST, tc::sdesc_sw128(aK + 32 * k, 16, 1024), tc::sdesc_sw128(aQ + 32 * k, 16, 1024),
+                        id_s, k > 0);
+#pragma unroll
+        for (int k = 0; k < HD / 16; ++k)
+          tc::umma_bf16(tmem + TM_DPT, tc::sdesc_sw128(aV + 32 * k, 16, 1024),
+                        tc::sdesc_sw128(aDO + 32 * k, 16, 1024), id_s, k > 0);
+        tc::umma_commit(bar_s_full);
+        return true;
+      };
+      if (ok) ok = issue_sdp(0);
+      for (int j = 0; ok && j < nq; ++j) {
+        const int s = j & 1;
+        if (!tc::mbar_wait(bar_p_full, j & 1, abort_flag, err)) break;
+        tc::tc_fence_after();
+        const uint32_t aQ = tc::smem_addr(smem + OFF_Q + s * TILE), aDO = tc::smem_addr(smem + OFF_DO + s * TILE);
+#pragma unroll
+        for (int k = 0; k < BQ / 16; ++k) {
+          const uint32_t koff = (k >> 2) * (128 * 128) + (k & 3) * 32;  // K-major A: 64-query column blocks
+          tc::umma_bf16(tmem + TM_DV, tc::sdesc_sw128(aPT + koff, 16, 1024),
+                        tc::sdesc_sw128(aDO + k * 2048, 128 * 128, 1024), id_kv, (j > 0 || k > 0) ? 1u : 0u);
+          tc::umma_bf16(tmem + TM_DK, tc::sdesc_sw128(aDST + koff, 16, 1024),
+                        tc::sdesc_sw128(aQ + k * 2048, 128 * 128, 1024), id_kv, (j > 0 || k > 0) ? 1u : 0u);
+        }
+        if (j > 0) {
+          if (!tc::mbar_wait(bar_dq_free, (j - 1) & 1, abort_flag, err)) break;
+          tc::tc_fence_after();
+        }
+#pragma unroll
+        for (int k = 0; k < BN / 16; ++k)
+          tc::umma_bf16(tmem + TM_DQ, tc::sdesc_sw128(aDST + k * 2048, 128 * 128, 1024),
+                        tc::sdesc_sw128(aK + k * 2048, 128 * 128, 1024), id_q, k > 0);
+        tc::umma_commit(bar_mma_done);
+        tc::umma_commit(bar_q_empty + s);
+        if (j + 1 < nq && !issue_sdp(j + 1)) break;
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ key-row threads
+    const int r = threadIdx.x;  // key row within the tile == TMEM lane
+    const int jk = n0 + r;      // combined key index
+    const uint32_t tl = tmem + ((uint32_t)(warp * 32) << 16);
+    uint8_t* sPT = smem + OFF_PT;
+    uint8_t* sDST = smem + OFF_DST;
+    bool ok = true;
+    auto drain_dq = [&](int jb) {
+      const int q0 = (qs + jb) * BQ;
+      const int i = q0 + r;  // the dQ TMEM lane is the query row
+#pragma unroll
+      for (int hh = 0; hh < HD / 32; ++hh) {
+        uint32_t v[32];
+        tc::tmem_ld32(tl + TM_DQ + hh * 32, v);
+        tc::tmem_wait_ld();
+        if (i < Tn) {
+          float* dst = dQa + ((int64_t)bh * Tn + i) * HD + hh * 32;
+#pragma unroll
+          for (int x = 0; x < 32; x += 4)
+            tc::red_add4(dst + x, __uint_as_float(v[x]) * scale, __uint_as_float(v[x + 1]) * scale,
+                         __uint_as_float(v[x + 2]) * scale, __uint_as_float(v[x + 3]) * scale);
+        }
+      }
+    };
+    for (int jb = 0; jb < nq; ++jb) {
+      const int s = jb & 1;
+      const int q0 = (qs + jb) * BQ;
+      ok = tc::mbar_wait(bar_s_full, jb & 1, abort_flag, err);
+      if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+      if (jb > 0) {
+        // MMAs of the previous block done: P^T/dS^T buffers free, its dQ ready
+        ok = tc::mbar_wait(bar_mma_done, (jb - 1) & 1, abort_flag, err);
+        if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+        tc::tc_fence_after();
+        drain_dq(jb - 1);
+        tc::tc_fence_before();
+        tc::mbar_arrive(bar_dq_free);
+      }
+      tc::tc_fence_after();
+      // visible query columns [c_lo, c_hi) of this key row in this block
+      int c_lo = 0, c_hi = 0;
+      if (jk < P) {
+        c_hi = min(BQ, Tn - q0);
+      } else if (jk < L) {
+        const int jm = jk - P;
+        c_lo = min(BQ, max(0, jm - q0));
+        c_hi = max(c_lo, min(BQ, min(Tn - 1, jm + W - 1) - q0 + 1));
+      }
+      const float* sl = reinterpret_cast<const float*>(smem + OFF_L + s * BQ * 4);
+      const float* sd = reinterpret_cast<const float*>(smem + OFF_D + s * BQ * 4);
+#pragma unroll
+      for (int c = 0; c < BQ / 32; ++c) {
+        uint32_t st[32], dp[32];
+        tc::tmem_ld32(tl + TM_ST + c * 32, st);
+        tc::tmem_ld32(tl + TM_DPT + c * 32, dp);
+        tc::tmem_wait_ld();
+        uint32_t pp[16], dd[16];
+#pragma unroll
+        for (int x = 0; x < 32; x += 2) {
+          const int c0 = c * 32 + x;
+          const float p0 = (c0 >= c_lo && c0 < c_hi) ? ex2(fmaf(__uint_as_float(st[x]), scale_log2, -sl[c0])) : 0.f;
+          const float p1 =
+              (c0 + 1 >= c_lo && c0 + 1 < c_hi) ? ex2(fmaf(__uint_as_float(st[x + 1]), scale_log2, -sl[c0 + 1])) : 0.f;
+          pp[x >> 1] = pack2(p0, p1);
+          dd[x >> 1] = pack2(p0 * (__uint_as_float(dp[x]) - sd[c0]), p1 * (__uint_as_float(dp[x + 1]) - sd[c0 + 1]));
+        }
+        const int cb = c >> 1;  // 64-query column block
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int ch = (c & 1) * 4 + q;
+          const int off = cb * (128 * 128) + r * 128 + ((ch ^ (r & 7)) << 4);
+          *reinterpret_cast<uint4*>(sPT + off) = make_uint4(pp[4 * q], pp[4 * q + 1], pp[4 * q + 2], pp[4 * q + 3]);
+          *reinterpret_cast<uint4*>(sDST + off) = make_uint4(dd[4 * q], dd[4 * q + 1], dd[4 * q + 2], dd[4 * q + 3]);
+        }
+      }
+      tc::fence_proxy_async_smem();
+      tc::tc_fence_before();
+      tc::mbar_arrive(bar_p_full);
+    }
+    if (ok) {
+      ok = tc::mbar_wait(bar_mma_done, (nq - 1) & 1, abort_flag, err);
+      if (__all_sync(0xffffffffu, ok)) {
+        tc::tc_fence_after();
+        drain_dq(nq - 1);
+        // dK (scaled) and dV rows of this key tile
+#pragma unroll
+        for (int which = 0; which < 2; ++which) {
+          float* base = which == 0 ? dKa : dVa;
+          const float mul = which == 0 ? scale : 1.f;
+#pragma unroll
+          for (int hh = 0; hh < HD / 32; ++hh) {
+            uint32_t v[32];
+            tc::tmem_ld32(tl + (which == 0 ? TM_DK : TM_DV) + hh * 32, v);
+            tc::tmem_wait_ld();
+            if (jk < L) {
+              float* dst = base + ((int64_t)bh * L + jk) * HD + hh * 32;
+#pragma unroll
+              for (int x = 0; x < 32; x += 4)
+                tc::red_add4(dst + x, __uint_as_float(v[x]) * mul, __uint_as_float(v[x + 1]) * mul,
+                             __uint_as_float(v[x + 2]) * mul, __uint_as_float(v[x + 3]) * mul);
+            }
+          }
+        }
+      }
+    }
+  }
+
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  if (warp == 5) tc::tmem_dealloc(tmem, TM_COLS);
+}
+
+CUtensorMap make_map_dO(const void* base, int B, int Tn, int H) {
+  CUtensorMap m;
+  cuuint64_t dims[4] = {(cuuint64_t)HD, (cuuint64_t)H, (cuuint64_t)Tn, (cuuint64_t)B};
+  cuuint64_t strides[3] = {(cuuint64_t)HD * 2, (cuuint64_t)H * HD * 2, (cuuint64_t)Tn * H * HD * 2};
+  cuuint32_t box[4] = {64, 1, (cuuint32_t)BQ, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = attn_tc::encode_tiled_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims,
+                                          strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                          CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (dO) failed: ", (int)r);
+  return m;
+}
+
+}  // namespace attn_tcb
+
+// Same contract as attn_bwd_packed (head_dim 64): returns {dQa, dKa, dVa} fp32.
+std::vector<at::Tensor> attn_bwd_tc(const at::Tensor& dO_in, const at::Tensor& Q, const at::Tensor& K,
+                                    const at::Tensor& V, const at::Tensor& O, const at::Tensor& LSE, int64_t window,
+                                    double scale) {
+  using namespace attn_tcb;
+  const at::cuda::CUDAGuard g(Q.device());
+  const int B = Q.size(0), H = Q.size(1), Tn = Q.size(2), hd = Q.size(3);
+  TORCH_CHECK(hd == HD, "attn_bwd_tc: head_dim must be 64");
+  const int L = K.size(2), P = L - Tn;
+  at::Tensor dO = dO_in.to(at::kBFloat16).contiguous();
+  TORCH_CHECK(dO.sizes() == O.sizes() && aligned16(dO) && aligned16(Q) && aligned16(K) && aligned16(V),
+              "attn_bwd_tc: layout");
+  auto f32 = Q.options().dtype(at::kFloat);
+  at::Tensor dQa = at::zeros({B, H, Tn, HD}, f32);
+  at::Tensor dKa = at::zeros({B, H, L, HD}, f32);
+  at::Tensor dVa = at::zeros({B, H, L, HD}, f32);
+  if ((int64_t)B * H * Tn == 0) return {dQa, dKa, dVa};
+  const int Tpad = (Tn + BQ - 1) / BQ * BQ;
+  at::Tensor Dd = at::empty({B, H, Tpad}, f32);
+  at::Tensor L2 = at::empty({B, H, Tpad}, f32);
+  {
+    const int64_t work = (int64_t)B * H * Tpad * 8;
+    bwd_pre_tc_kernel<<<(work + 255) / 256, 256, 0, stream()>>>(
+        (const bf16*)dO.data_ptr(), (const bf16*)O.data_ptr(), LSE.data_ptr<float>(), Dd.data_ptr<float>(),
+        L2.data_ptr<float>(), B, H, Tn, Tpad);
+    check_launch("attn_bwd_tc pre");
+  }
+  const CUtensorMap mk = attn_tc::make_map_3d(K.data_ptr(), HD, L, (uint64_t)B * H, BN);
+  const CUtensorMap mv = attn_tc::make_map_3d(V.data_ptr(), HD, L, (uint64_t)B * H, BN);
+  const CUtensorMap mq = attn_tc::make_map_3d(Q.data_ptr(), HD, Tn, (uint64_t)B * H, BQ);
+  const CUtensorMap mdo = make_map_dO(dO.data_ptr(), B, Tn, H);
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaFuncSetAttribute(attn_bwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    attr_set = true;
+  }
+  const int W = (int)std::min<int64_t>(window, 1 << 30);
+  const int nkt = (L + BN - 1) / BN;
+  const int max_qb = (Tn + BQ - 1) / BQ + 1;
+  const int splits = std::max(1, (max_qb + QB_PER_SPLIT - 1) / QB_PER_SPLIT);
+  dim3 grid(nkt * splits, B * H);
+  attn_bwd_tc_kernel<<<grid, 192, SMEM_BYTES, stream()>>>(
+      mk, mv, mq, mdo, L2.data_ptr<float>(), Dd.data_ptr<float>(), dQa.data_ptr<float>(), dKa.data_ptr<float>(),
+      dVa.data_ptr<float>(), H, Tn, Tpad, P, W, (float)scale, (float)scale * 1.4426950408889634f, splits,
+      (unsigned*)tc_error_word(Q.device()).data_ptr<int>());
+  check_launch("attn_bwd_tc");
+  return {dQa, dKa, dVa};
+}
+
+}  // namespace tb

@@ -49,6 +49,9 @@ std::vector<at::Tensor> attn_unpack(const at::Tensor& dQa, const at::Tensor& dKa
 std::vector<at::Tensor> attn_fwd_tc(const at::Tensor& Q, const at::Tensor& K, const at::Tensor& V, int64_t window,
                                     double scale);
 bool attn_tc_supported(int64_t head_dim);
+std::vector<at::Tensor> attn_bwd_tc(const at::Tensor& dO, const at::Tensor& Q, const at::Tensor& K,
+                                    const at::Tensor& V, const at::Tensor& O, const at::Tensor& LSE, int64_t window,
+                                    double scale);
 int64_t kernel_error_status(int64_t device, bool reset);
 }  // namespace tb
 
@@ -75,5 +78,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_unpack", &tb::attn_unpack);
   m.def("attn_fwd_tc", &tb::attn_fwd_tc);
   m.def("attn_tc_supported", &tb::attn_tc_supported);
+  m.def("attn_bwd_tc", &tb::attn_bwd_tc);
   m.def("kernel_error_status", &tb::kernel_error_status, pybind11::arg("device") = 0, pybind11::arg("reset") = true);
 }

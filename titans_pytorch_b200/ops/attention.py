@@ -108,7 +108,10 @@ class _WindowAttnFn(torch.autograd.Function):
     def backward(ctx, dO):
         Q, K, V, O, lse, inv_freq = ctx.saved_tensors
         E = ext()
-        dQa, dKa, dVa = E.attn_bwd_packed(dO, Q, K, V, O, lse, ctx.window, ctx.scale)
+        if E.attn_tc_supported(Q.shape[-1]):
+            dQa, dKa, dVa = E.attn_bwd_tc(dO, Q, K, V, O, lse, ctx.window, ctx.scale)      # tcgen05
+        else:
+            dQa, dKa, dVa = E.attn_bwd_packed(dO, Q, K, V, O, lse, ctx.window, ctx.scale)  # mma.sync
         dqkv, dpkv = E.attn_unpack(dQa, dKa, dVa, inv_freq, max(ctx.bp, 1), ctx.dtype)
         return dqkv, (dpkv if ctx.bp else None), None, None, None, None
 

@@ -53,6 +53,17 @@ std::vector<at::Tensor> attn_bwd_tc(const at::Tensor& dO, const at::Tensor& Q, c
                                     const at::Tensor& V, const at::Tensor& O, const at::Tensor& LSE, int64_t window,
                                     double scale);
 int64_t kernel_error_status(int64_t device, bool reset);
+// comm.cu
+std::vector<at::Tensor> comm_alloc(int64_t nbytes, int64_t device);
+int64_t comm_ipc_open(const at::Tensor& handle, int64_t device);
+void comm_ipc_close(int64_t ptr);
+void comm_barrier(const at::Tensor& sig_ptrs, int64_t slot, int64_t epoch, int64_t world, int64_t me, at::Tensor& err);
+void comm_reduce_shard(const at::Tensor& grad_ptrs, int64_t lo, int64_t n, at::Tensor& gsum, double gscale,
+                       const at::Tensor& slot_ptrs, int64_t world, int64_t me);
+void comm_adamw_shard(const at::Tensor& gsum, at::Tensor& master, at::Tensor& exp_avg, at::Tensor& exp_avg_sq,
+                      const at::Tensor& param_ptrs, int64_t lo, int64_t world, const at::Tensor& tab, int64_t nseg,
+                      int64_t items, const at::Tensor& norm_slots, double gscale, double max_norm, double lr,
+                      double beta1, double beta2, double eps, double wd, int64_t step, at::Tensor& norm_out);
 }  // namespace tb
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -79,5 +90,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_fwd_tc", &tb::attn_fwd_tc);
   m.def("attn_tc_supported", &tb::attn_tc_supported);
   m.def("attn_bwd_tc", &tb::attn_bwd_tc);
+  m.def("comm_alloc", &tb::comm_alloc);
+  m.def("comm_ipc_open", &tb::comm_ipc_open);
+  m.def("comm_ipc_close", &tb::comm_ipc_close);
+  m.def("comm_barrier", &tb::comm_barrier);
+  m.def("comm_reduce_shard", &tb::comm_reduce_shard);
+  m.def("comm_adamw_shard", &tb::comm_adamw_shard);
   m.def("kernel_error_status", &tb::kernel_error_status, pybind11::arg("device") = 0, pybind11::arg("reset") = true);
 }

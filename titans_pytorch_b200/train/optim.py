@@ -30,17 +30,37 @@ from ..ops._ext import ext, want_kernels
 ALIGN = 64  # elements; keeps every parameter view 128-byte aligned for bf16
 
 
+def unique_trainable(params) -> list:
+    """Trainable parameters in order, each once (tied weights appear once)."""
+    seen, plist = set(), []
+    for p in params:
+        if p.requires_grad and id(p) not in seen:
+            seen.add(id(p))
+            plist.append(p)
+    if not plist:
+        raise ValueError("no trainable parameters")
+    return plist
+
+
+def intersect_segments(segs, lo: int, hi: int) -> list[tuple[int, int]]:
+    """Active (offset, length) ranges clipped to [lo, hi), made relative to lo."""
+    out = []
+    for o, n in segs:
+        a, b = max(o, lo), min(o + n, hi)
+        if a < b:
+            out.append((a - lo, b - a))
+    return out
+
+
 class FlatParamSpace:
     """Owns the flat parameter and gradient buffers of a set of parameters."""
 
-    def __init__(self, params, grad_dtype: torch.dtype | None = None) -> None:
-        seen, plist = set(), []
-        for p in params:
-            if p.requires_grad and id(p) not in seen:
-                seen.add(id(p))
-                plist.append(p)
-        if not plist:
-            raise ValueError("no trainable parameters")
+    def __init__(self, params, grad_dtype: torch.dtype | None = None, pad_to: int = 1,
+                 buffers=None) -> None:
+        """``pad_to``: round the total length up to a multiple of it (e.g. ALIGN*world for
+        sharding).  ``buffers``: optional callable ``(total, dtype) -> (flat, grad)`` that
+        provides the two flat buffers (e.g. peer-visible memory); zero-filled."""
+        plist = unique_trainable(params)
         self.params = plist
         self.device = plist[0].device
         self.dtype = plist[0].dtype
@@ -50,9 +70,12 @@ class FlatParamSpace:
         for p in plist:
             self.offsets.append(off)
             off += (p.numel() + ALIGN - 1) // ALIGN * ALIGN
-        self.total = off
-        self.flat = torch.zeros(self.total, dtype=self.dtype, device=self.device)
-        self.grad = torch.zeros(self.total, dtype=grad_dtype or self.dtype, device=self.device)
+        self.total = (off + pad_to - 1) // pad_to * pad_to
+        if buffers is not None:
+            self.flat, self.grad = buffers(self.total, self.dtype)
+        else:
+            self.flat = torch.zeros(self.total, dtype=self.dtype, device=self.device)
+            self.grad = torch.zeros(self.total, dtype=grad_dtype or self.dtype, device=self.device)
         with torch.no_grad():
             for p, o in zip(plist, self.offsets):
                 n = p.numel()

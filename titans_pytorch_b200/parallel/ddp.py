@@ -186,6 +186,8 @@ class DataParallelEngine:
         self.reduce = reduce
 
     def make_optimizer(self, model: torch.nn.Module, cfg):
+        if self.reduce == "fused" and next(model.parameters()).dtype != torch.bfloat16:
+            self.reduce = "collective"  # the peer-memory path exchanges bf16 weights and gradients
         if self.reduce == "fused":
             return FusedDPAdamW(model, cfg, self.group)
         opt = DPFusedAdamW(model.parameters(), lr=cfg.lr, betas=cfg.betas, eps=cfg.eps,

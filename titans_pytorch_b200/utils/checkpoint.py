@@ -1,0 +1,120 @@
+"""Checkpoints in the reference's formats.
+
+The reference's loaders (`scripts/inference.py:130-165`,
+`scripts/eval_perplexity.py:87-94`, `scripts/benchmark_babilong.py:104-111`)
+read ``TitansConfig(**ckpt["config"])``, ``ckpt["model_type"]`` and
+``ckpt["model_state_dict"]``.  :func:`save_checkpoint` writes exactly that (the
+config restricted to the reference's fields, the tied ``head.weight`` present
+as in ``state_dict()``), plus the training state the reference's trainer
+stores (`scripts/pretrain.py:657-672`: optimizer, scheduler, scaler, step,
+epoch, best val loss) and the resume extras it lacks (RNG states, data
+position).  :func:`load_checkpoint` also reads the reference's own trainer
+checkpoints, whose ``config`` is the trainer's flag dict and which have no
+``model_type`` (inferred from the state-dict keys), and strips the
+``_orig_mod.`` prefix torch.compile leaves on keys.
+"""
+
+from __future__ import annotations
+
+import os
+import random
+from typing import Any
+
+import numpy as np
+import torch
+
+from ..config import TitansConfig
+from ..models.titans import MODEL_CLASSES
+
+
+def infer_model_type(state_dict: dict[str, torch.Tensor]) -> str:
+    keys = state_dict.keys()
+    if any(".norm_mem." in k for k in keys):
+        return "mac"
+    if any(".norm3." in k for k in keys):
+        return "mal"
+    if not any(".attention." in k for k in keys):
+        return "lmm"
+    return "mag"
+
+
+def _clean(sd: dict[str, torch.Tensor]) -> dict[str, torch.Tensor]:
+    return {k.removeprefix("_orig_mod.").removeprefix("module."): v for k, v in sd.items()}
+
+
+def rng_state() -> dict[str, Any]:
+    st = {"python": random.getstate(), "numpy": np.random.get_state(), "torch": torch.get_rng_state()}
+    if torch.cuda.is_available():
+        st["cuda"] = torch.cuda.get_rng_state_all()
+    return st
+
+
+def set_rng_state(st: dict[str, Any]) -> None:
+    random.setstate(st["python"])
+    np.random.set_state(st["numpy"])
+    torch.set_rng_state(st["torch"])
+    if "cuda" in st and torch.cuda.is_available():
+        torch.cuda.set_rng_state_all(st["cuda"])
+
+
+def save_checkpoint(path: str, model: torch.nn.Module, optimizer=None, scheduler=None, *, global_step: int = 0,
+                    epoch: int = 0, best_val_loss: float = float("inf"), model_type: str | None = None,
+                    tokenizer_name: str | None = None, data_position: int | None = None,
+                    train_config: dict | None = None, dtype: torch.dtype | None = None) -> str:
+    """Write a reference-loadable checkpoint (plus resume state) to ``path``."""
+    cfg: TitansConfig = model.config
+    sd = {k: (v.to(dtype) if dtype is not None and v.is_floating_point() else v).detach().cpu()
+          for k, v in model.state_dict().items()}
+    ckpt = {
+        "model_state_dict": sd,
+        "optimizer_state_dict": optimizer.state_dict() if optimizer is not None else None,
+        "scheduler_state_dict": scheduler.state_dict() if scheduler is not None else None,
+        "scaler_state_dict": None,
+        "global_step": global_step,
+        "epoch": epoch,
+        "best_val_loss": best_val_loss,
+        "config": cfg.to_dict(reference_only=True),
+        "titans_b200_config": cfg.to_dict(),
+        "model_type": model_type or getattr(model, "model_type", infer_model_type(sd)),
+        "rng_state": rng_state(),
+        "data_position": data_position,
+        "train_config": train_config,
+    }
+    if tokenizer_name is not None:
+        ckpt["tokenizer_name"] = tokenizer_name
+    os.makedirs(os.path.dirname(os.path.abspath(path)), exist_ok=True)
+    tmp = path + ".tmp"
+    torch.save(ckpt, tmp)
+    os.replace(tmp, path)  # never leave a truncated checkpoint behind
+    return path
+
+
+def load_model(path: str, device=None, dtype: torch.dtype | None = None, **config_overrides):
+    """Build the model a checkpoint describes and load its weights; returns (model, ckpt)."""
+    ckpt = torch.load(path, map_location="cpu", weights_only=False)
+    if not isinstance(ckpt, dict) or "model_state_dict" not in ckpt:
+        raise ValueError(f"{path}: not a Titans checkpoint (no model_state_dict)")
+    sd = _clean(ckpt["model_state_dict"])
+    raw = ckpt.get("titans_b200_config") or ckpt.get("config") or {}
+    cfg = TitansConfig.from_dict({**raw, **config_overrides})
+    kind = ckpt.get("model_type") or infer_model_type(sd)
+    model = MODEL_CLASSES[kind](cfg)
+    model.load_state_dict(sd, strict=True)
+    model = model.to(device=device, dtype=dtype) if (device or dtype) else model
+    return model, ckpt
+
+
+def load_checkpoint(path: str, model: torch.nn.Module, optimizer=None, scheduler=None,
+                    restore_rng: bool = True, map_location="cpu") -> dict:
+    """Restore weights (and optimizer / scheduler / RNG when given); returns the checkpoint dict."""
+    ckpt = torch.load(path, map_location=map_location, weights_only=False)
+    sd = _clean(ckpt["model_state_dict"])
+    with torch.no_grad():
+        model.load_state_dict({k: v.to(model.state_dict()[k].dtype) for k, v in sd.items()}, strict=True)
+    if optimizer is not None and ckpt.get("optimizer_state_dict") is not None:
+        optimizer.load_state_dict(ckpt["optimizer_state_dict"])
+    if scheduler is not None and ckpt.get("scheduler_state_dict") is not None:
+        scheduler.load_state_dict(ckpt["scheduler_state_dict"])
+    if restore_rng and ckpt.get("rng_state") is not None:
+        set_rng_state(ckpt["rng_state"])
+    return ckpt

@@ -1,0 +1,235 @@
+"""Runtime utilities: device timers, NVTX ranges, memory stats, model benchmarks,
+activation checkpointing and CUDA-graph capture.
+
+Counterparts of the reference's helpers (`src/titans/cuda_optimizations.py:378-759`,
+`src/titans/optimized_training.py:428-603`) with B200-specific choices:
+
+* ``compile_model`` does not run torch.compile; it returns a
+  :class:`CUDAGraphRunner` that captures the model's forward for fixed input
+  shapes and replays it (launch overhead is the cost torch.compile's
+  ``reduce-overhead`` mode targets).
+* ``configure_memory_pool`` does **not** claim a fraction of the GPU (the
+  reference sets 0.95, which starves other processes on a shared device); it
+  only sets allocator options that take effect before the first allocation.
+* timing is CUDA events on the launching stream, never wall clock.
+"""
+
+from __future__ import annotations
+
+import contextlib
+import os
+import subprocess
+import time
+
+import torch
+
+try:  # NVTX ranges for nsys/ncu timelines
+    import torch.cuda.nvtx as _nvtx
+except Exception:  # pragma: no cover
+    _nvtx = None
+
+
+@contextlib.contextmanager
+def nvtx_range(name: str):
+    if _nvtx is not None and torch.cuda.is_available():
+        _nvtx.range_push(name)
+        try:
+            yield
+        finally:
+            _nvtx.range_pop()
+    else:
+        yield
+
+
+class CudaTimer:
+    """Accumulates device time of regions with CUDA events (read with ``.ms``)."""
+
+    def __init__(self) -> None:
+        self.events: list[tuple[torch.cuda.Event, torch.cuda.Event]] = []
+
+    @contextlib.contextmanager
+    def region(self):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        yield
+        e.record()
+        self.events.append((s, e))
+
+    @property
+    def ms(self) -> float:
+        torch.cuda.synchronize()
+        return sum(s.elapsed_time(e) for s, e in self.events)
+
+
+@contextlib.contextmanager
+def profile_cuda(name: str = "profile", enabled: bool = True, sink=print):
+    """Print the device time of the enclosed region (CUDA events)."""
+    if not enabled or not torch.cuda.is_available():
+        yield
+        return
+    t = CudaTimer()
+    with nvtx_range(name), t.region():
+        yield
+    sink(f"{name}: {t.ms:.3f} ms")
+
+
+def get_gpu_memory_stats(device=None) -> dict[str, float]:
+    if not torch.cuda.is_available():
+        return {}
+    gb = 1024 ** 3
+    return {"allocated_gb": torch.cuda.memory_allocated(device) / gb,
+            "reserved_gb": torch.cuda.memory_reserved(device) / gb,
+            "max_allocated_gb": torch.cuda.max_memory_allocated(device) / gb}
+
+
+def print_gpu_utilization() -> str:
+    """nvidia-smi utilisation / memory / clocks (read-only query)."""
+    try:
+        out = subprocess.run(["nvidia-smi", "--query-gpu=index,utilization.gpu,memory.used,memory.total,"
+                              "clocks.sm,clocks.max.sm,power.draw", "--format=csv"],
+                             capture_output=True, text=True, timeout=10).stdout
+    except (OSError, subprocess.SubprocessError) as e:
+        out = f"nvidia-smi unavailable: {e}"
+    print(out)
+    return out
+
+
+def configure_memory_pool(expandable_segments: bool = True) -> None:
+    """Allocator options only (no per-process memory fraction on shared GPUs)."""
+    if expandable_segments and "PYTORCH_CUDA_ALLOC_CONF" not in os.environ:
+        os.environ["PYTORCH_CUDA_ALLOC_CONF"] = "expandable_segments:True"
+
+
+def empty_cache_if_needed(threshold: float = 0.9) -> None:
+    if torch.cuda.is_available():
+        free, total = torch.cuda.mem_get_info()
+        if 1 - free / total > threshold:
+            torch.cuda.empty_cache()
+
+
+def enable_gradient_checkpointing(model: torch.nn.Module) -> torch.nn.Module:
+    """Recompute each block's forward in the backward (non-reentrant checkpoint).
+
+    The memory update inside a block runs without autograd and is a pure
+    function of the block input, so recomputation reproduces it exactly.
+    """
+    from torch.utils.checkpoint import checkpoint
+
+    for block in getattr(model, "blocks", []):
+        if getattr(block, "_titans_ckpt", False):
+            continue
+        fwd = block.forward
+
+        def wrapped(x, state=None, _fwd=fwd):
+            return checkpoint(_fwd, x, state, use_reentrant=False)
+
+        block.forward = wrapped
+        block._titans_ckpt = True
+    return model
+
+
+class CUDAGraphRunner:
+    """Capture ``fn(*static_inputs)`` once and replay it; inputs are copied into static buffers."""
+
+    def __init__(self, fn, example_inputs: tuple[torch.Tensor, ...], warmup: int = 2) -> None:
+        self.fn = fn
+        self.static_in = tuple(x.clone() for x in example_inputs)
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            for _ in range(warmup):
+                fn(*self.static_in)
+        torch.cuda.current_stream().wait_stream(s)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.static_out = fn(*self.static_in)
+
+    def __call__(self, *inputs: torch.Tensor):
+        for dst, src in zip(self.static_in, inputs):
+            dst.copy_(src, non_blocking=True)
+        self.graph.replay()
+        return self.static_out
+
+
+def compile_model(model: torch.nn.Module, example_input_ids: torch.Tensor | None = None, **_ignored):
+    """Inference forward captured as a CUDA graph for ``example_input_ids``'s shape
+    (returns the model unchanged without an example or without CUDA)."""
+    if example_input_ids is None or not torch.cuda.is_available():
+        return model
+    model.eval()
+
+    @torch.no_grad()
+    def fwd(ids):
+        return model(ids)[0]
+
+    return CUDAGraphRunner(fwd, (example_input_ids,))
+
+
+def compile_function(fn, *_args, **_kw):
+    return fn
+
+
+@torch.no_grad()
+def benchmark_model(model: torch.nn.Module, batch_size: int = 4, seq_len: int = 256, warmup: int = 3,
+                    iters: int = 10, vocab_size: int | None = None) -> dict[str, float]:
+    """Forward latency (ms) and tokens/s, device-timed."""
+    dev = next(model.parameters()).device
+    ids = torch.randint(0, vocab_size or model.config.vocab_size, (batch_size, seq_len), device=dev)
+    model.eval()
+    for _ in range(warmup):
+        model(ids)
+    if dev.type == "cuda":
+        t = CudaTimer()
+        with t.region():
+            for _ in range(iters):
+                model(ids)
+        ms = t.ms / iters
+    else:
+        t0 = time.perf_counter()
+        for _ in range(iters):
+            model(ids)
+        ms = (time.perf_counter() - t0) * 1000 / iters
+    return {"latency_ms": ms, "tokens_per_s": batch_size * seq_len / (ms / 1000)}
+
+
+def get_optimal_batch_size(model: torch.nn.Module, seq_len: int, max_batch: int = 256,
+                           memory_fraction: float = 0.8) -> int:
+    """Largest power-of-two batch whose training step fits in ``memory_fraction`` of free memory."""
+    if not torch.cuda.is_available():
+        return 1
+    dev = next(model.parameters()).device
+    best, b = 1, 1
+    free0 = torch.cuda.mem_get_info(dev)[0]
+    while b <= max_batch:
+        try:
+            torch.cuda.reset_peak_memory_stats(dev)
+            base = torch.cuda.memory_allocated(dev)
+            ids = torch.randint(0, model.config.vocab_size, (b, seq_len), device=dev)
+            logits, _ = model(ids)
+            logits.float().mean().backward()
+            model.zero_grad(set_to_none=True)
+            if torch.cuda.max_memory_allocated(dev) - base > memory_fraction * free0:
+                break
+            best = b
+            b *= 2
+        except torch.cuda.OutOfMemoryError:
+            break
+        finally:
+            torch.cuda.empty_cache()
+    return best
+
+
+def is_triton_available() -> bool:
+    """The framework's kernels are native CUDA; Triton is never used."""
+    return False
+
+
+def is_flash_attention_available() -> bool:
+    """True: attention runs on the framework's own sm_100a flash kernels."""
+    from ..ops._ext import available
+
+    return available()
+
+
+def is_torch_sdpa_available() -> bool:
+    return hasattr(torch.nn.functional, "scaled_dot_product_attention")

@@ -415,9 +415,10 @@ namespace tb {
 // One CTA = one (batch, head), one tile of 128 keys (the M dimension of the
 // key-major products) and a range of 128-query blocks (the queries that can see
 // those keys; the prefix tile, seen by every query, is split across CTAs).
-// 6 warps: warp 4 TMA producer (K, V once; Q, dO, log-sum-exp and D per query
-// block through a 2-stage ring), warp 5 TMEM allocator + MMA issuer, warps 0..3
-// one thread per key row (= TMEM lane).  Per query block:
+// 10 warps: warp 8 TMA producer (K, V once; Q, dO, log-sum-exp and D per query
+// block through a 2-stage ring), warp 9 TMEM allocator + MMA issuer, warps 0..7
+// two warpgroups of key-row threads (thread = key row = TMEM lane; the two
+// warpgroups split the query columns).  Per query block:
 //   S^T  = K Q^T      (M=128 keys, N=128 queries, K=64)      -> TMEM
 //   dP^T = V dO^T     (M=128, N=128, K=64)                    -> TMEM
 //   threads: P^T = exp2(S^T*scale*log2e - lse2), dS^T = P^T (dP^T - D), both
@@ -481,7 +482,7 @@ __global__ void bwd_pre_tc_kernel(const bf16* __restrict__ dO, const bf16* __res
   }
 }
 
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(320, 1)
     attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                        const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmDO,
                        const float* __restrict__ L2, const float* __restrict__ Dd, float* __restrict__ dQa,
@@ -532,13 +533,13 @@ __global__ void __launch_bounds__(192, 1)
       tc::mbar_init(bar_q_empty + s, 1);
     }
     tc::mbar_init(bar_s_full, 1);
-    tc::mbar_init(bar_p_full, 128);
+    tc::mbar_init(bar_p_full, 256);
     tc::mbar_init(bar_mma_done, 1);
-    tc::mbar_init(bar_dq_free, 128);
+    tc::mbar_init(bar_dq_free, 256);
     *abort_flag = 0;
     tc::mbar_fence_init();
   }
-  if (warp == 5) {
+  if (warp == 9) {
     tc::tmem_alloc(tmem_slot, TM_COLS);
     tc::tmem_relinquish();
   }
@@ -547,7 +548,7 @@ __global__ void __launch_bounds__(192, 1)
   tc::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 4) {
+  if (warp == 8) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       tc::mbar_expect_tx(bar_kv, 2 * TILE);
@@ -572,7 +573,7 @@ __global__ void __launch_bounds__(192, 1)
           tc::mbar_wait(bar_q_full + (j & 1), (j >> 1) & 1, &keep_waiting, nullptr, 1ll << 27);
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == 9) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t id_s = tc::idesc_bf16_f32(128, 128, false, false);
@@ -626,17 +627,20 @@ __global__ void __launch_bounds__(192, 1)
     }
   } else {
     // ------------------------------------------------------------ key-row threads
-    const int r = threadIdx.x;  // key row within the tile == TMEM lane
-    const int jk = n0 + r;      // combined key index
-    const uint32_t tl = tmem + ((uint32_t)(warp * 32) << 16);
+    // two warpgroups: both cover all 128 key rows (TMEM lanes); warpgroup wg
+    // handles query columns [64 wg, 64 wg + 64) and dQ/dK/dV column half wg.
+    const int wg = warp >> 2;
+    const int r = threadIdx.x & 127;  // key row within the tile == TMEM lane
+    const int jk = n0 + r;            // combined key index
+    const uint32_t tl = tmem + ((uint32_t)((warp & 3) * 32) << 16);
     uint8_t* sPT = smem + OFF_PT;
     uint8_t* sDST = smem + OFF_DST;
     bool ok = true;
     auto drain_dq = [&](int jb) {
       const int q0 = (qs + jb) * BQ;
       const int i = q0 + r;  // the dQ TMEM lane is the query row
-#pragma unroll
-      for (int hh = 0; hh < HD / 32; ++hh) {
+      {
+        const int hh = wg;  // this warpgroup's 32 of the 64 dQ columns
         uint32_t v[32];
         tc::tmem_ld32(tl + TM_DQ + hh * 32, v);
         tc::tmem_wait_ld();
@@ -676,7 +680,8 @@ __global__ void __launch_bounds__(192, 1)
       const float* sl = reinterpret_cast<const float*>(smem + OFF_L + s * BQ * 4);
       const float* sd = reinterpret_cast<const float*>(smem + OFF_D + s * BQ * 4);
 #pragma unroll
-      for (int c = 0; c < BQ / 32; ++c) {
+      for (int cc = 0; cc < 2; ++cc) {
+        const int c = wg * 2 + cc;  // 32-query chunk handled by this warpgroup
         uint32_t st[32], dp[32];
         tc::tmem_ld32(tl + TM_ST + c * 32, st);
         tc::tmem_ld32(tl + TM_DPT + c * 32, dp);
@@ -709,9 +714,9 @@ __global__ void __launch_bounds__(192, 1)
       if (__all_sync(0xffffffffu, ok)) {
         tc::tc_fence_after();
         drain_dq(nq - 1);
-        // dK (scaled) and dV rows of this key tile
-#pragma unroll
-        for (int which = 0; which < 2; ++which) {
+        // dK (scaled, warpgroup 0) and dV (warpgroup 1) rows of this key tile
+        {
+          const int which = wg;
           float* base = which == 0 ? dKa : dVa;
           const float mul = which == 0 ? scale : 1.f;
 #pragma unroll
@@ -735,7 +740,7 @@ __global__ void __launch_bounds__(192, 1)
   tc::tc_fence_before();
   __syncthreads();
   tc::tc_fence_after();
-  if (warp == 5) tc::tmem_dealloc(tmem, TM_COLS);
+  if (warp == 9) tc::tmem_dealloc(tmem, TM_COLS);
 }
 
 CUtensorMap make_map_dO(const void* base, int B, int Tn, int H) {
@@ -795,7 +800,7 @@ std::vector<at::Tensor> attn_bwd_tc(const at::Tensor& dO_in, const at::Tensor& Q
   const int max_qb = (Tn + BQ - 1) / BQ + 1;
   const int splits = std::max(1, (max_qb + QB_PER_SPLIT - 1) / QB_PER_SPLIT);
   dim3 grid(nkt * splits, B * H);
-  attn_bwd_tc_kernel<<<grid, 192, SMEM_BYTES, stream()>>>(
+  attn_bwd_tc_kernel<<<grid, 320, SMEM_BYTES, stream()>>>(
       mk, mv, mq, mdo, L2.data_ptr<float>(), Dd.data_ptr<float>(), dQa.data_ptr<float>(), dKa.data_ptr<float>(),
       dVa.data_ptr<float>(), H, Tn, Tpad, P, W, (float)scale, (float)scale * 1.4426950408889634f, splits,
       (unsigned*)tc_error_word(Q.device()).data_ptr<int>());

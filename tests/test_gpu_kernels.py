@@ -231,7 +231,10 @@ def test_attention_tcgen05_forward(case):
     assert float((l_tc - lse_ref).abs().max()) < 2e-2
 
 
-@pytest.mark.parametrize("case", TC_CASES + [(1, 2, 1100, 4, 512), (2, 1, 700, 16, 100)])
+# the last two: several work items per persistent CTA (B*H*items > SM count),
+# with no-window tiles split over several items
+@pytest.mark.parametrize("case", TC_CASES + [(1, 2, 1100, 4, 512), (2, 1, 700, 16, 100), (4, 8, 1024, 4, 256),
+                                             (2, 4, 2048, 8, 1 << 30)])
 def test_attention_tcgen05_backward(case):
     """tcgen05 backward vs the mma.sync backward (both against the same forward outputs)."""
     B, H, T, P, W = case

@@ -23,6 +23,10 @@
 // CTA's window, so work is O(T * (P + window)).  Every mbarrier wait is
 // bounded; on a timeout the CTA records an error code and unwinds (TMEM is
 // always released).
+#include <map>
+#include <mutex>
+#include <tuple>
+
 #include "tc_common.cuh"
 
 namespace tb {
@@ -410,38 +414,51 @@ std::vector<at::Tensor> attn_fwd_tc(const at::Tensor& Q, const at::Tensor& K, co
 namespace tb {
 
 // =============================================================================
-// Backward, head_dim 64, on tcgen05.
+// Backward, head_dim 64, on tcgen05: a persistent kernel.
 //
-// One CTA = one (batch, head), one tile of 128 keys (the M dimension of the
-// key-major products) and a range of 128-query blocks (the queries that can see
-// those keys; the prefix tile, seen by every query, is split across CTAs).
-// 10 warps: warp 8 TMA producer (K, V once; Q, dO, log-sum-exp and D per query
-// block through a 2-stage ring), warp 9 TMEM allocator + MMA issuer, warps 0..7
-// two warpgroups of key-row threads (thread = key row = TMEM lane; the two
-// warpgroups split the query columns).  Per query block:
-//   S^T  = K Q^T      (M=128 keys, N=128 queries, K=64)      -> TMEM
-//   dP^T = V dO^T     (M=128, N=128, K=64)                    -> TMEM
-//   threads: P^T = exp2(S^T*scale*log2e - lse2), dS^T = P^T (dP^T - D), both
-//            written as bf16 into shared memory in the UMMA K-major layout
-//   dV  += P^T dO     (M=128 keys, N=64, K=128; dO as an MN-major operand)
-//   dK  += dS^T Q     (same shapes; Q as an MN-major operand)
-//   dQ   = dS K       (M=128 queries, N=64, K=128 keys; dS read as an MN-major
-//                      operand straight from the dS^T tile, K as MN-major)
-//   threads: dQ rows (TMEM lanes = queries) -> red.global.add.v4.f32 into dQa
-// At the end dK (scaled) and dV rows go to dKa / dVa with vector reductions
-// (a key tile can be shared by several CTAs).  All waits are bounded.
+// Work item = one (batch, head), one tile of 128 keys (the M dimension of the
+// key-major products) and a run of 128-query blocks that can see those keys
+// (the tile holding the prefix keys, seen by every query, is split over
+// several items).  The host builds the item list once per (T, P, window); each
+// CTA (one per SM) walks items blockIdx.x, blockIdx.x + gridDim.x, ...
+// 10 warps:
+//   warp 8      TMA producer: K, V of each item into one of two slots (so the
+//               next item's tiles land while this one finishes), and Q, dO,
+//               log-sum-exp and D of each query block through a 2-stage ring;
+//   warp 9      TMEM allocator + single-thread MMA issuer;
+//   warps 0..7  two warpgroups of key-row threads: thread = key row = TMEM
+//               lane; warpgroup w handles query columns [64w, 64w+64) of the
+//               score tiles and column half w of the dQ / dK|dV drains.
+// Per query block g (one global sequence over the CTA's items):
+//   S^T  = K Q^T, dP^T = V dO^T     (M=128 keys, N=128 queries, K=64) -> TMEM
+//   threads: P^T = exp2(S^T*scale*log2e - lse2), dS^T = P^T (dP^T - D) into
+//            registers; release S^T/dP^T (s_free); store both as bf16 into
+//            shared memory in the UMMA K-major layout (p_full); drain the
+//            previous block's dQ rows (TMEM lane = query) with
+//            red.global.add.v4.f32 into dQa (dq_free)
+//   dV  += P^T dO, dK += dS^T Q     (M=128 keys, N=64, K=128; dO / Q MN-major)
+//   dQ   = dS K                     (after dq_free; M=128 queries, N=64,
+//                                    K=128 keys; dS read MN-major from the
+//                                    dS^T tile)
+// The MMA warp issues S/dP of block g+1 as soon as the threads have released
+// block g's scores, so the tensor core computes the next scores while the
+// threads store P/dS and drain dQ.  At the end of an item dK (scaled) and dV
+// rows are stored (plain stores; vector reductions into rows zeroed by the
+// pre-pass when the key tile is split over several items).
+// All waits are bounded: a timeout records an error code and every role
+// unwinds; TMEM is always released.
 // =============================================================================
 namespace attn_tcb {
 
 using bf16 = __nv_bfloat16;
 constexpr int HD = 64, BN = 128, BQ = 128;
 constexpr int TILE = 128 * 64 * 2;  // 16 KB: one [128 rows][64 bf16] swizzled tile
-constexpr int OFF_K = 0, OFF_V = OFF_K + TILE, OFF_Q = OFF_V + TILE, OFF_DO = OFF_Q + 2 * TILE;
+constexpr int OFF_K = 0, OFF_V = OFF_K + 2 * TILE, OFF_Q = OFF_V + 2 * TILE, OFF_DO = OFF_Q + 2 * TILE;
 constexpr int OFF_PT = OFF_DO + 2 * TILE, OFF_DST = OFF_PT + 2 * TILE;
 constexpr int OFF_L = OFF_DST + 2 * TILE, OFF_D = OFF_L + 2 * BQ * 4, OFF_BAR = OFF_D + 2 * BQ * 4;
 constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;
 constexpr uint32_t TM_ST = 0, TM_DPT = 128, TM_DV = 256, TM_DK = 320, TM_DQ = 384, TM_COLS = 512;
-constexpr int QB_PER_SPLIT = 6;
+constexpr int QB_PER_SPLIT = 6;  // query blocks per item of a split key tile
 
 __device__ __forceinline__ uint32_t pack2(float a, float b) {
   __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
@@ -453,18 +470,37 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
-// D[bh, i] = sum_d dO * O, lse2 = LSE * log2(e); both [BH][Tpad], zero padded.
+// 128-query blocks [qb_lo, qb_hi] that can see the key tile starting at
+// combined key index n0 (P prefix keys, then the T sequence keys).
+__host__ __device__ inline void tile_query_blocks(int n0, int P, int Tn, int W, int& qb_lo, int& qb_hi) {
+  int q_lo, q_hi;
+  if (n0 < P) {
+    q_lo = 0;
+    q_hi = Tn - 1;
+  } else {
+    const int last_key = (n0 + BN < P + Tn ? n0 + BN : P + Tn) - 1 - P;
+    q_lo = n0 - P;
+    q_hi = last_key + W - 1 < Tn - 1 ? last_key + W - 1 : Tn - 1;
+  }
+  qb_lo = q_lo / BQ;
+  qb_hi = q_hi / BQ;
+}
+
+// D[bh, i] = sum_d dO * O and lse2 = LSE * log2(e) (both [BH][Tpad], zero
+// padded); also zeroes the dQ accumulator and the dK/dV rows of split key
+// tiles.  8 threads per row, RP rows per (batch, head).
 __global__ void bwd_pre_tc_kernel(const bf16* __restrict__ dO, const bf16* __restrict__ O,
                                   const float* __restrict__ LSE, float* __restrict__ Dd, float* __restrict__ L2,
-                                  int B, int H, int Tn, int Tpad) {
-  const int64_t rows = (int64_t)B * H * Tpad;
-  const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;  // 8 threads per row
+                                  float* __restrict__ dQa, float* __restrict__ dKa, float* __restrict__ dVa, int B,
+                                  int H, int Tn, int Tpad, int P, int W, int RP) {
+  const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const int64_t r = e >> 3;
   const int c = (int)(e & 7);
+  const int64_t bh = r / RP;
+  const int i = (int)(r - bh * RP);
+  const bool live = bh < (int64_t)B * H;
   float acc = 0.f;
-  const int i = (int)(r % Tpad);
-  const int64_t bh = r / Tpad;
-  if (r < rows && i < Tn) {
+  if (live && i < Tn) {
     const int b = (int)(bh / H), h = (int)(bh % H);
     const int64_t off = (((int64_t)b * Tn + i) * H + h) * HD + c * 8;
     float a[8], o[8];
@@ -476,63 +512,96 @@ __global__ void bwd_pre_tc_kernel(const bf16* __restrict__ dO, const bf16* __res
   acc += __shfl_xor_sync(0xffffffffu, acc, 1);
   acc += __shfl_xor_sync(0xffffffffu, acc, 2);
   acc += __shfl_xor_sync(0xffffffffu, acc, 4);
-  if (r < rows && c == 0) {
-    Dd[r] = acc;
-    L2[r] = i < Tn ? LSE[bh * Tn + i] * 1.4426950408889634f : 0.f;
+  if (!live) return;
+  if (i < Tpad && c == 0) {
+    Dd[bh * Tpad + i] = acc;
+    L2[bh * Tpad + i] = i < Tn ? LSE[bh * Tn + i] * 1.4426950408889634f : 0.f;
+  }
+  const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (i < Tn) {
+    float4* q = reinterpret_cast<float4*>(dQa + (bh * Tn + i) * HD + c * 8);
+    q[0] = z;
+    q[1] = z;
+  }
+  if (i < P + Tn) {
+    int lo, hi;
+    tile_query_blocks(i / BN * BN, P, Tn, W, lo, hi);
+    if (hi - lo + 1 > QB_PER_SPLIT) {
+      const int64_t off = (bh * (P + Tn) + i) * HD + c * 8;
+      reinterpret_cast<float4*>(dKa + off)[0] = z;
+      reinterpret_cast<float4*>(dKa + off)[1] = z;
+      reinterpret_cast<float4*>(dVa + off)[0] = z;
+      reinterpret_cast<float4*>(dVa + off)[1] = z;
+    }
   }
 }
+
+// Walks the query blocks of a CTA's items in order: item i = blockIdx.x,
+// blockIdx.x + gridDim.x, ...; `it` counts the CTA's items, j the block within
+// the item.  items[p] = {key tile, first query block, query blocks, split}.
+struct Cursor {
+  const int4* items;
+  int n_pat, n_items, step;
+  int i, it, j, nq, qs, n0, bh, split;
+  __device__ Cursor(const int4* items_, int n_pat_, int n_items_)
+      : items(items_), n_pat(n_pat_), n_items(n_items_), step(gridDim.x), i(blockIdx.x), it(0), j(0) {
+    load();
+  }
+  __device__ void load() {
+    if (i < n_items) {
+      bh = i / n_pat;
+      const int4 w = items[i - bh * n_pat];
+      n0 = w.x * BN;
+      qs = w.y;
+      nq = w.z;
+      split = w.w;
+    }
+  }
+  __device__ bool valid() const { return i < n_items; }
+  __device__ void next() {
+    if (++j == nq) {
+      j = 0;
+      i += step;
+      ++it;
+      load();
+    }
+  }
+};
 
 __global__ void __launch_bounds__(320, 1)
     attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                        const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmDO,
-                       const float* __restrict__ L2, const float* __restrict__ Dd, float* __restrict__ dQa,
-                       float* __restrict__ dKa, float* __restrict__ dVa, int H, int Tn, int Tpad, int P, int W,
-                       float scale, float scale_log2, int splits, unsigned* __restrict__ err) {
-  const int bh = blockIdx.y;
-  const int kt = blockIdx.x / splits, sp = blockIdx.x % splits;
-  const int n0 = kt * BN;
+                       const int4* __restrict__ items, int n_pat, int n_items, const float* __restrict__ L2,
+                       const float* __restrict__ Dd, float* __restrict__ dQa, float* __restrict__ dKa,
+                       float* __restrict__ dVa, int H, int Tn, int Tpad, int P, int W, float scale,
+                       float scale_log2, unsigned* __restrict__ err) {
+  if ((int)blockIdx.x >= n_items) return;
   const int L = P + Tn;
-  if (n0 >= L) return;
-  // query range that can see this key tile
-  int q_lo, q_hi;
-  if (n0 < P) {
-    q_lo = 0;
-    q_hi = Tn - 1;
-  } else {
-    q_lo = n0 - P;
-    q_hi = min(Tn - 1, min(n0 + BN, L) - 1 - P + W - 1);
-  }
-  const int qb_lo = q_lo / BQ, qb_hi = q_hi / BQ;
-  const int nqb = qb_hi - qb_lo + 1;
-  const int nsp = min(splits, (nqb + QB_PER_SPLIT - 1) / QB_PER_SPLIT);
-  if (sp >= nsp) return;
-  const int per = (nqb + nsp - 1) / nsp;
-  const int qs = qb_lo + sp * per, qe = min(qb_hi + 1, qs + per);
-  const int nq = qe - qs;
-  if (nq <= 0) return;
-
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
-  uint64_t* bar_kv = bars + 0;
-  uint64_t* bar_q_full = bars + 1;   // [2]
-  uint64_t* bar_q_empty = bars + 3;  // [2]
-  uint64_t* bar_s_full = bars + 5;
-  uint64_t* bar_p_full = bars + 6;
-  uint64_t* bar_mma_done = bars + 7;
-  uint64_t* bar_dq_free = bars + 8;
+  uint64_t* bar_kv_full = bars + 0;   // [2] K/V slot loaded
+  uint64_t* bar_kv_empty = bars + 2;  // [2] K/V slot no longer read
+  uint64_t* bar_q_full = bars + 4;    // [2]
+  uint64_t* bar_q_empty = bars + 6;   // [2]
+  uint64_t* bar_s_full = bars + 8;    // S^T, dP^T of the current block in TMEM
+  uint64_t* bar_s_free = bars + 9;    // threads have read them
+  uint64_t* bar_p_full = bars + 10;   // P^T, dS^T in shared memory; previous dQ drained
+  uint64_t* bar_mma_done = bars + 11; // dV, dK, dQ of the block complete
+  uint64_t* bar_dq_free = bars + 12;  // previous block's dQ drained
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int b = bh / H, h = bh % H;
 
   if (threadIdx.x == 0) {
-    tc::mbar_init(bar_kv, 1);
     for (int s = 0; s < 2; ++s) {
+      tc::mbar_init(bar_kv_full + s, 1);
+      tc::mbar_init(bar_kv_empty + s, 1);
       tc::mbar_init(bar_q_full + s, 1);
       tc::mbar_init(bar_q_empty + s, 1);
     }
     tc::mbar_init(bar_s_full, 1);
+    tc::mbar_init(bar_s_free, 256);
     tc::mbar_init(bar_p_full, 256);
     tc::mbar_init(bar_mma_done, 1);
     tc::mbar_init(bar_dq_free, 256);
@@ -551,26 +620,37 @@ __global__ void __launch_bounds__(320, 1)
   if (warp == 8) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
-      tc::mbar_expect_tx(bar_kv, 2 * TILE);
-      tc::tma_load_3d(smem + OFF_K, &tmK, bar_kv, 0, n0, bh);
-      tc::tma_load_3d(smem + OFF_V, &tmV, bar_kv, 0, n0, bh);
-      int issued = 0;
-      for (int j = 0; j < nq; ++j) {
-        const int s = j & 1;
-        if (j >= 2 && !tc::mbar_wait(bar_q_empty + s, ((j >> 1) - 1) & 1, abort_flag, err)) break;
-        const int q0 = (qs + j) * BQ;
+      Cursor cur(items, n_pat, n_items);
+      int g = 0, kv_issued = 0;
+      bool ok = true;
+      while (ok && cur.valid()) {
+        if (cur.j == 0) {
+          const int slot = cur.it & 1;
+          if (cur.it >= 2 && !tc::mbar_wait(bar_kv_empty + slot, ((cur.it >> 1) - 1) & 1, abort_flag, err)) break;
+          tc::mbar_expect_tx(bar_kv_full + slot, 2 * TILE);
+          tc::tma_load_3d(smem + OFF_K + slot * TILE, &tmK, bar_kv_full + slot, 0, cur.n0, cur.bh);
+          tc::tma_load_3d(smem + OFF_V + slot * TILE, &tmV, bar_kv_full + slot, 0, cur.n0, cur.bh);
+          ++kv_issued;
+        }
+        const int s = g & 1;
+        if (g >= 2 && !tc::mbar_wait(bar_q_empty + s, ((g >> 1) - 1) & 1, abort_flag, err)) break;
+        const int q0 = (cur.qs + cur.j) * BQ;
+        const int b = cur.bh / H, h = cur.bh - b * H;
         tc::mbar_expect_tx(bar_q_full + s, 2 * TILE + 2 * BQ * 4);
-        tc::tma_load_3d(smem + OFF_Q + s * TILE, &tmQ, bar_q_full + s, 0, q0, bh);
+        tc::tma_load_3d(smem + OFF_Q + s * TILE, &tmQ, bar_q_full + s, 0, q0, cur.bh);
         tc::tma_load_4d(smem + OFF_DO + s * TILE, &tmDO, bar_q_full + s, 0, h, q0, b);
-        tc::bulk_load(smem + OFF_L + s * BQ * 4, L2 + (int64_t)bh * Tpad + q0, BQ * 4, bar_q_full + s);
-        tc::bulk_load(smem + OFF_D + s * BQ * 4, Dd + (int64_t)bh * Tpad + q0, BQ * 4, bar_q_full + s);
-        issued = j + 1;
+        tc::bulk_load(smem + OFF_L + s * BQ * 4, L2 + (int64_t)cur.bh * Tpad + q0, BQ * 4, bar_q_full + s);
+        tc::bulk_load(smem + OFF_D + s * BQ * 4, Dd + (int64_t)cur.bh * Tpad + q0, BQ * 4, bar_q_full + s);
+        ++g;
+        cur.next();
       }
       if (*abort_flag) {
+        // let the copies already issued land before the CTA exits
         volatile int keep_waiting = 0;
-        tc::mbar_wait(bar_kv, 0, &keep_waiting, nullptr, 1ll << 27);
-        for (int j = max(0, issued - 2); j < issued; ++j)
-          tc::mbar_wait(bar_q_full + (j & 1), (j >> 1) & 1, &keep_waiting, nullptr, 1ll << 27);
+        for (int t = max(0, kv_issued - 2); t < kv_issued; ++t)
+          tc::mbar_wait(bar_kv_full + (t & 1), (t >> 1) & 1, &keep_waiting, nullptr, 1ll << 27);
+        for (int t = max(0, g - 2); t < g; ++t)
+          tc::mbar_wait(bar_q_full + (t & 1), (t >> 1) & 1, &keep_waiting, nullptr, 1ll << 27);
       }
     }
   } else if (warp == 9) {
@@ -579,13 +659,14 @@ __global__ void __launch_bounds__(320, 1)
       constexpr uint32_t id_s = tc::idesc_bf16_f32(128, 128, false, false);
       constexpr uint32_t id_kv = tc::idesc_bf16_f32(128, HD, false, true);  // dV, dK: B (dO / Q) MN-major
       constexpr uint32_t id_q = tc::idesc_bf16_f32(128, HD, true, true);    // dQ: A (dS) and B (K) MN-major
-      const uint32_t aK = tc::smem_addr(smem + OFF_K), aV = tc::smem_addr(smem + OFF_V);
+      const uint32_t aK0 = tc::smem_addr(smem + OFF_K), aV0 = tc::smem_addr(smem + OFF_V);
       const uint32_t aPT = tc::smem_addr(smem + OFF_PT), aDST = tc::smem_addr(smem + OFF_DST);
-      bool ok = tc::mbar_wait(bar_kv, 0, abort_flag, err);
-      auto issue_sdp = [&](int j) -> bool {
-        const int s = j & 1;
-        if (!tc::mbar_wait(bar_q_full + s, (j >> 1) & 1, abort_flag, err)) return false;
+      auto issue_sdp = [&](const Cursor& c, int gg) -> bool {
+        const int s = gg & 1, slot = c.it & 1;
+        if (c.j == 0 && !tc::mbar_wait(bar_kv_full + slot, (c.it >> 1) & 1, abort_flag, err)) return false;
+        if (!tc::mbar_wait(bar_q_full + s, (gg >> 1) & 1, abort_flag, err)) return false;
         tc::tc_fence_after();
+        const uint32_t aK = aK0 + slot * TILE, aV = aV0 + slot * TILE;
         const uint32_t aQ = tc::smem_addr(smem + OFF_Q + s * TILE), aDO = tc::smem_addr(smem + OFF_DO + s * TILE);
 #pragma unroll
         for (int k = 0; k < HD / 16; ++k)
@@ -598,75 +679,68 @@ __global__ void __launch_bounds__(320, 1)
         tc::umma_commit(bar_s_full);
         return true;
       };
-      if (ok) ok = issue_sdp(0);
-      for (int j = 0; ok && j < nq; ++j) {
-        const int s = j & 1;
-        if (!tc::mbar_wait(bar_p_full, j & 1, abort_flag, err)) break;
+      Cursor cur(items, n_pat, n_items);
+      bool ok = issue_sdp(cur, 0);
+      for (int g = 0; ok && cur.valid(); ++g) {
+        if (!tc::mbar_wait(bar_s_free, g & 1, abort_flag, err)) break;
         tc::tc_fence_after();
+        Cursor nxt = cur;
+        nxt.next();
+        if (nxt.valid() && !issue_sdp(nxt, g + 1)) break;
+        if (!tc::mbar_wait(bar_p_full, g & 1, abort_flag, err)) break;
+        tc::tc_fence_after();
+        const int s = g & 1, slot = cur.it & 1;
+        const uint32_t aK = aK0 + slot * TILE;
         const uint32_t aQ = tc::smem_addr(smem + OFF_Q + s * TILE), aDO = tc::smem_addr(smem + OFF_DO + s * TILE);
 #pragma unroll
         for (int k = 0; k < BQ / 16; ++k) {
           const uint32_t koff = (k >> 2) * (128 * 128) + (k & 3) * 32;  // K-major A: 64-query column blocks
+          const uint32_t acc = (cur.j > 0 || k > 0) ? 1u : 0u;
           tc::umma_bf16(tmem + TM_DV, tc::sdesc_sw128(aPT + koff, 16, 1024),
-                        tc::sdesc_sw128(aDO + k * 2048, 128 * 128, 1024), id_kv, (j > 0 || k > 0) ? 1u : 0u);
+                        tc::sdesc_sw128(aDO + k * 2048, 128 * 128, 1024), id_kv, acc);
           tc::umma_bf16(tmem + TM_DK, tc::sdesc_sw128(aDST + koff, 16, 1024),
-                        tc::sdesc_sw128(aQ + k * 2048, 128 * 128, 1024), id_kv, (j > 0 || k > 0) ? 1u : 0u);
+                        tc::sdesc_sw128(aQ + k * 2048, 128 * 128, 1024), id_kv, acc);
         }
-        if (j > 0) {
-          if (!tc::mbar_wait(bar_dq_free, (j - 1) & 1, abort_flag, err)) break;
-          tc::tc_fence_after();
-        }
+        if (!tc::mbar_wait(bar_dq_free, g & 1, abort_flag, err)) break;
+        tc::tc_fence_after();
 #pragma unroll
         for (int k = 0; k < BN / 16; ++k)
           tc::umma_bf16(tmem + TM_DQ, tc::sdesc_sw128(aDST + k * 2048, 128 * 128, 1024),
                         tc::sdesc_sw128(aK + k * 2048, 128 * 128, 1024), id_q, k > 0);
         tc::umma_commit(bar_mma_done);
         tc::umma_commit(bar_q_empty + s);
-        if (j + 1 < nq && !issue_sdp(j + 1)) break;
+        if (cur.j == cur.nq - 1) tc::umma_commit(bar_kv_empty + slot);
+        cur = nxt;
       }
     }
   } else {
     // ------------------------------------------------------------ key-row threads
-    // two warpgroups: both cover all 128 key rows (TMEM lanes); warpgroup wg
-    // handles query columns [64 wg, 64 wg + 64) and dQ/dK/dV column half wg.
     const int wg = warp >> 2;
     const int r = threadIdx.x & 127;  // key row within the tile == TMEM lane
-    const int jk = n0 + r;            // combined key index
     const uint32_t tl = tmem + ((uint32_t)((warp & 3) * 32) << 16);
     uint8_t* sPT = smem + OFF_PT;
     uint8_t* sDST = smem + OFF_DST;
-    bool ok = true;
-    auto drain_dq = [&](int jb) {
-      const int q0 = (qs + jb) * BQ;
-      const int i = q0 + r;  // the dQ TMEM lane is the query row
-      {
-        const int hh = wg;  // this warpgroup's 32 of the 64 dQ columns
-        uint32_t v[32];
-        tc::tmem_ld32(tl + TM_DQ + hh * 32, v);
-        tc::tmem_wait_ld();
-        if (i < Tn) {
-          float* dst = dQa + ((int64_t)bh * Tn + i) * HD + hh * 32;
+    // dQ rows of query block q0 (TMEM lane = query row), column half wg
+    auto drain_dq = [&](int bh, int q0) {
+      const int i = q0 + r;
+      uint32_t v[32];
+      tc::tmem_ld32(tl + TM_DQ + wg * 32, v);
+      tc::tmem_wait_ld();
+      if (i < Tn) {
+        float* dst = dQa + ((int64_t)bh * Tn + i) * HD + wg * 32;
 #pragma unroll
-          for (int x = 0; x < 32; x += 4)
-            tc::red_add4(dst + x, __uint_as_float(v[x]) * scale, __uint_as_float(v[x + 1]) * scale,
-                         __uint_as_float(v[x + 2]) * scale, __uint_as_float(v[x + 3]) * scale);
-        }
+        for (int x = 0; x < 32; x += 4)
+          tc::red_add4(dst + x, __uint_as_float(v[x]) * scale, __uint_as_float(v[x + 1]) * scale,
+                       __uint_as_float(v[x + 2]) * scale, __uint_as_float(v[x + 3]) * scale);
       }
     };
-    for (int jb = 0; jb < nq; ++jb) {
-      const int s = jb & 1;
-      const int q0 = (qs + jb) * BQ;
-      ok = tc::mbar_wait(bar_s_full, jb & 1, abort_flag, err);
-      if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
-      if (jb > 0) {
-        // MMAs of the previous block done: P^T/dS^T buffers free, its dQ ready
-        ok = tc::mbar_wait(bar_mma_done, (jb - 1) & 1, abort_flag, err);
-        if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
-        tc::tc_fence_after();
-        drain_dq(jb - 1);
-        tc::tc_fence_before();
-        tc::mbar_arrive(bar_dq_free);
-      }
+    Cursor cur(items, n_pat, n_items);
+    for (int g = 0; cur.valid(); ++g) {
+      const int s = g & 1;
+      const int q0 = (cur.qs + cur.j) * BQ;
+      const int jk = cur.n0 + r;  // combined key index of this thread's row
+      bool ok = tc::mbar_wait(bar_s_full, g & 1, abort_flag, err);
+      if (!__all_sync(0xffffffffu, ok)) break;
       tc::tc_fence_after();
       // visible query columns [c_lo, c_hi) of this key row in this block
       int c_lo = 0, c_hi = 0;
@@ -679,6 +753,7 @@ __global__ void __launch_bounds__(320, 1)
       }
       const float* sl = reinterpret_cast<const float*>(smem + OFF_L + s * BQ * 4);
       const float* sd = reinterpret_cast<const float*>(smem + OFF_D + s * BQ * 4);
+      uint32_t pp[32], dd[32];
 #pragma unroll
       for (int cc = 0; cc < 2; ++cc) {
         const int c = wg * 2 + cc;  // 32-query chunk handled by this warpgroup
@@ -686,54 +761,79 @@ __global__ void __launch_bounds__(320, 1)
         tc::tmem_ld32(tl + TM_ST + c * 32, st);
         tc::tmem_ld32(tl + TM_DPT + c * 32, dp);
         tc::tmem_wait_ld();
-        uint32_t pp[16], dd[16];
 #pragma unroll
         for (int x = 0; x < 32; x += 2) {
           const int c0 = c * 32 + x;
           const float p0 = (c0 >= c_lo && c0 < c_hi) ? ex2(fmaf(__uint_as_float(st[x]), scale_log2, -sl[c0])) : 0.f;
           const float p1 =
               (c0 + 1 >= c_lo && c0 + 1 < c_hi) ? ex2(fmaf(__uint_as_float(st[x + 1]), scale_log2, -sl[c0 + 1])) : 0.f;
-          pp[x >> 1] = pack2(p0, p1);
-          dd[x >> 1] = pack2(p0 * (__uint_as_float(dp[x]) - sd[c0]), p1 * (__uint_as_float(dp[x + 1]) - sd[c0 + 1]));
+          pp[cc * 16 + (x >> 1)] = pack2(p0, p1);
+          dd[cc * 16 + (x >> 1)] =
+              pack2(p0 * (__uint_as_float(dp[x]) - sd[c0]), p1 * (__uint_as_float(dp[x + 1]) - sd[c0 + 1]));
         }
+      }
+      tc::tc_fence_before();
+      tc::mbar_arrive(bar_s_free);
+      if (cur.j > 0) {
+        // MMAs of the previous block done: P^T/dS^T buffers free, its dQ ready
+        ok = tc::mbar_wait(bar_mma_done, (g - 1) & 1, abort_flag, err);
+        if (!__all_sync(0xffffffffu, ok)) break;
+        tc::tc_fence_after();
+      }
+#pragma unroll
+      for (int cc = 0; cc < 2; ++cc) {
+        const int c = wg * 2 + cc;
         const int cb = c >> 1;  // 64-query column block
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           const int ch = (c & 1) * 4 + q;
           const int off = cb * (128 * 128) + r * 128 + ((ch ^ (r & 7)) << 4);
-          *reinterpret_cast<uint4*>(sPT + off) = make_uint4(pp[4 * q], pp[4 * q + 1], pp[4 * q + 2], pp[4 * q + 3]);
-          *reinterpret_cast<uint4*>(sDST + off) = make_uint4(dd[4 * q], dd[4 * q + 1], dd[4 * q + 2], dd[4 * q + 3]);
+          const int u = cc * 16 + 4 * q;
+          *reinterpret_cast<uint4*>(sPT + off) = make_uint4(pp[u], pp[u + 1], pp[u + 2], pp[u + 3]);
+          *reinterpret_cast<uint4*>(sDST + off) = make_uint4(dd[u], dd[u + 1], dd[u + 2], dd[u + 3]);
         }
       }
       tc::fence_proxy_async_smem();
       tc::tc_fence_before();
       tc::mbar_arrive(bar_p_full);
-    }
-    if (ok) {
-      ok = tc::mbar_wait(bar_mma_done, (nq - 1) & 1, abort_flag, err);
-      if (__all_sync(0xffffffffu, ok)) {
+      if (cur.j > 0) {
+        drain_dq(cur.bh, q0 - BQ);
+        tc::tc_fence_before();
+      }
+      tc::mbar_arrive(bar_dq_free);
+      if (cur.j == cur.nq - 1) {
+        // last block of the item: its dQ, then the item's dK (scaled,
+        // warpgroup 0) and dV (warpgroup 1) rows
+        ok = tc::mbar_wait(bar_mma_done, g & 1, abort_flag, err);
+        if (!__all_sync(0xffffffffu, ok)) break;
         tc::tc_fence_after();
-        drain_dq(nq - 1);
-        // dK (scaled, warpgroup 0) and dV (warpgroup 1) rows of this key tile
-        {
-          const int which = wg;
-          float* base = which == 0 ? dKa : dVa;
-          const float mul = which == 0 ? scale : 1.f;
+        drain_dq(cur.bh, q0);
+        float* base = wg == 0 ? dKa : dVa;
+        const float mul = wg == 0 ? scale : 1.f;
 #pragma unroll
-          for (int hh = 0; hh < HD / 32; ++hh) {
-            uint32_t v[32];
-            tc::tmem_ld32(tl + (which == 0 ? TM_DK : TM_DV) + hh * 32, v);
-            tc::tmem_wait_ld();
-            if (jk < L) {
-              float* dst = base + ((int64_t)bh * L + jk) * HD + hh * 32;
+        for (int hh = 0; hh < HD / 32; ++hh) {
+          uint32_t v[32];
+          tc::tmem_ld32(tl + (wg == 0 ? TM_DK : TM_DV) + hh * 32, v);
+          tc::tmem_wait_ld();
+          if (jk < L) {
+            float* dst = base + ((int64_t)cur.bh * L + jk) * HD + hh * 32;
+            if (cur.split) {
 #pragma unroll
               for (int x = 0; x < 32; x += 4)
                 tc::red_add4(dst + x, __uint_as_float(v[x]) * mul, __uint_as_float(v[x + 1]) * mul,
                              __uint_as_float(v[x + 2]) * mul, __uint_as_float(v[x + 3]) * mul);
+            } else {
+#pragma unroll
+              for (int x = 0; x < 32; x += 4)
+                *reinterpret_cast<float4*>(dst + x) =
+                    make_float4(__uint_as_float(v[x]) * mul, __uint_as_float(v[x + 1]) * mul,
+                                __uint_as_float(v[x + 2]) * mul, __uint_as_float(v[x + 3]) * mul);
             }
           }
         }
+        tc::tc_fence_before();
       }
+      cur.next();
     }
   }
 
@@ -757,6 +857,34 @@ CUtensorMap make_map_dO(const void* base, int B, int Tn, int H) {
   return m;
 }
 
+// Work items {key tile, first query block, query blocks, split} for one
+// (T, P, window); the same list serves every (batch, head).  Cached per
+// device and shape (built on the host once, then copied to the device).
+const at::Tensor& work_items(const at::Device& dev, int Tn, int P, int W) {
+  static std::mutex mu;
+  static std::map<std::tuple<int, int, int, int>, at::Tensor> cache;
+  std::lock_guard<std::mutex> lock(mu);
+  const auto key = std::make_tuple((int)dev.index(), Tn, P, W);
+  auto it = cache.find(key);
+  if (it != cache.end()) return it->second;
+  std::vector<int32_t> v;
+  const int nkt = (P + Tn + BN - 1) / BN;
+  for (int kt = 0; kt < nkt; ++kt) {
+    int lo, hi;
+    tile_query_blocks(kt * BN, P, Tn, W, lo, hi);
+    const int nqb = hi - lo + 1;
+    const int nsp = (nqb + QB_PER_SPLIT - 1) / QB_PER_SPLIT;
+    const int per = (nqb + nsp - 1) / nsp;
+    for (int sp = 0; sp < nsp; ++sp) {
+      const int qs = lo + sp * per, qe = std::min(hi + 1, qs + per);
+      if (qe <= qs) continue;
+      v.insert(v.end(), {kt, qs, qe - qs, nsp > 1 ? 1 : 0});
+    }
+  }
+  at::Tensor host = at::from_blob(v.data(), {(int64_t)v.size() / 4, 4}, at::kInt).clone();
+  return cache.emplace(key, host.to(dev)).first->second;
+}
+
 }  // namespace attn_tcb
 
 // Same contract as attn_bwd_packed (head_dim 64): returns {dQa, dKa, dVa} fp32.
@@ -772,20 +900,29 @@ std::vector<at::Tensor> attn_bwd_tc(const at::Tensor& dO_in, const at::Tensor& Q
   TORCH_CHECK(dO.sizes() == O.sizes() && aligned16(dO) && aligned16(Q) && aligned16(K) && aligned16(V),
               "attn_bwd_tc: layout");
   auto f32 = Q.options().dtype(at::kFloat);
-  at::Tensor dQa = at::zeros({B, H, Tn, HD}, f32);
-  at::Tensor dKa = at::zeros({B, H, L, HD}, f32);
-  at::Tensor dVa = at::zeros({B, H, L, HD}, f32);
-  if ((int64_t)B * H * Tn == 0) return {dQa, dKa, dVa};
+  at::Tensor dQa = at::empty({B, H, Tn, HD}, f32);
+  at::Tensor dKa = at::empty({B, H, L, HD}, f32);
+  at::Tensor dVa = at::empty({B, H, L, HD}, f32);
+  if ((int64_t)B * H * Tn == 0) return {dQa.zero_(), dKa.zero_(), dVa.zero_()};
+  const int W = (int)std::min<int64_t>(window, 1 << 30);
   const int Tpad = (Tn + BQ - 1) / BQ * BQ;
+  const int nkt = (L + BN - 1) / BN;
+  const int RP = std::max(Tpad, nkt * BN);
   at::Tensor Dd = at::empty({B, H, Tpad}, f32);
   at::Tensor L2 = at::empty({B, H, Tpad}, f32);
   {
-    const int64_t work = (int64_t)B * H * Tpad * 8;
+    const int64_t work = (int64_t)B * H * RP * 8;
     bwd_pre_tc_kernel<<<(work + 255) / 256, 256, 0, stream()>>>(
         (const bf16*)dO.data_ptr(), (const bf16*)O.data_ptr(), LSE.data_ptr<float>(), Dd.data_ptr<float>(),
-        L2.data_ptr<float>(), B, H, Tn, Tpad);
+        L2.data_ptr<float>(), dQa.data_ptr<float>(), dKa.data_ptr<float>(), dVa.data_ptr<float>(), B, H, Tn, Tpad,
+        P, W, RP);
     check_launch("attn_bwd_tc pre");
   }
+  const at::Tensor& items = work_items(Q.device(), Tn, P, W);
+  const int n_pat = items.size(0);
+  const int64_t n_items64 = (int64_t)n_pat * B * H;
+  TORCH_CHECK(n_items64 < (1ll << 31), "attn_bwd_tc: too many work items");
+  const int n_items = (int)n_items64;
   const CUtensorMap mk = attn_tc::make_map_3d(K.data_ptr(), HD, L, (uint64_t)B * H, BN);
   const CUtensorMap mv = attn_tc::make_map_3d(V.data_ptr(), HD, L, (uint64_t)B * H, BN);
   const CUtensorMap mq = attn_tc::make_map_3d(Q.data_ptr(), HD, Tn, (uint64_t)B * H, BQ);
@@ -795,15 +932,11 @@ std::vector<at::Tensor> attn_bwd_tc(const at::Tensor& dO_in, const at::Tensor& Q
     cudaFuncSetAttribute(attn_bwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
     attr_set = true;
   }
-  const int W = (int)std::min<int64_t>(window, 1 << 30);
-  const int nkt = (L + BN - 1) / BN;
-  const int max_qb = (Tn + BQ - 1) / BQ + 1;
-  const int splits = std::max(1, (max_qb + QB_PER_SPLIT - 1) / QB_PER_SPLIT);
-  dim3 grid(nkt * splits, B * H);
+  const int grid = std::min(n_items, num_sms());
   attn_bwd_tc_kernel<<<grid, 320, SMEM_BYTES, stream()>>>(
-      mk, mv, mq, mdo, L2.data_ptr<float>(), Dd.data_ptr<float>(), dQa.data_ptr<float>(), dKa.data_ptr<float>(),
-      dVa.data_ptr<float>(), H, Tn, Tpad, P, W, (float)scale, (float)scale * 1.4426950408889634f, splits,
-      (unsigned*)tc_error_word(Q.device()).data_ptr<int>());
+      mk, mv, mq, mdo, reinterpret_cast<const int4*>(items.data_ptr<int>()), n_pat, n_items, L2.data_ptr<float>(),
+      Dd.data_ptr<float>(), dQa.data_ptr<float>(), dKa.data_ptr<float>(), dVa.data_ptr<float>(), H, Tn, Tpad, P, W,
+      (float)scale, (float)scale * 1.4426950408889634f, (unsigned*)tc_error_word(Q.device()).data_ptr<int>());
   check_launch("attn_bwd_tc");
   return {dQa, dKa, dVa};
 }

@@ -753,6 +753,8 @@ __global__ void __launch_bounds__(320, 1)
       }
       const float* sl = reinterpret_cast<const float*>(smem + OFF_L + s * BQ * 4);
       const float* sd = reinterpret_cast<const float*>(smem + OFF_D + s * BQ * 4);
+      // every query column of the block visible to this key row: no masking
+      const bool row_full = c_lo == 0 && c_hi == BQ;
       uint32_t pp[32], dd[32];
 #pragma unroll
       for (int cc = 0; cc < 2; ++cc) {
@@ -762,14 +764,24 @@ __global__ void __launch_bounds__(320, 1)
         tc::tmem_ld32(tl + TM_DPT + c * 32, dp);
         tc::tmem_wait_ld();
 #pragma unroll
-        for (int x = 0; x < 32; x += 2) {
+        for (int x = 0; x < 32; x += 4) {
           const int c0 = c * 32 + x;
-          const float p0 = (c0 >= c_lo && c0 < c_hi) ? ex2(fmaf(__uint_as_float(st[x]), scale_log2, -sl[c0])) : 0.f;
-          const float p1 =
-              (c0 + 1 >= c_lo && c0 + 1 < c_hi) ? ex2(fmaf(__uint_as_float(st[x + 1]), scale_log2, -sl[c0 + 1])) : 0.f;
-          pp[cc * 16 + (x >> 1)] = pack2(p0, p1);
+          const float4 l4 = *reinterpret_cast<const float4*>(sl + c0);
+          const float4 d4 = *reinterpret_cast<const float4*>(sd + c0);
+          float p[4] = {ex2(fmaf(__uint_as_float(st[x]), scale_log2, -l4.x)),
+                        ex2(fmaf(__uint_as_float(st[x + 1]), scale_log2, -l4.y)),
+                        ex2(fmaf(__uint_as_float(st[x + 2]), scale_log2, -l4.z)),
+                        ex2(fmaf(__uint_as_float(st[x + 3]), scale_log2, -l4.w))};
+          if (!row_full) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) p[e] = (c0 + e >= c_lo && c0 + e < c_hi) ? p[e] : 0.f;
+          }
+          pp[cc * 16 + (x >> 1)] = pack2(p[0], p[1]);
+          pp[cc * 16 + (x >> 1) + 1] = pack2(p[2], p[3]);
           dd[cc * 16 + (x >> 1)] =
-              pack2(p0 * (__uint_as_float(dp[x]) - sd[c0]), p1 * (__uint_as_float(dp[x + 1]) - sd[c0 + 1]));
+              pack2(p[0] * (__uint_as_float(dp[x]) - d4.x), p[1] * (__uint_as_float(dp[x + 1]) - d4.y));
+          dd[cc * 16 + (x >> 1) + 1] =
+              pack2(p[2] * (__uint_as_float(dp[x + 2]) - d4.z), p[3] * (__uint_as_float(dp[x + 3]) - d4.w));
         }
       }
       tc::tc_fence_before();

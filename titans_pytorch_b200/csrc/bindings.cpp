@@ -53,6 +53,9 @@ std::vector<at::Tensor> attn_bwd_tc(const at::Tensor& dO, const at::Tensor& Q, c
                                     const at::Tensor& V, const at::Tensor& O, const at::Tensor& LSE, int64_t window,
                                     double scale);
 int64_t kernel_error_status(int64_t device, bool reset);
+at::Tensor memory_scan_fwd(at::Tensor& W1, at::Tensor& S1, at::Tensor& W2T, at::Tensor& S2T, const at::Tensor& k,
+                           const at::Tensor& v, const at::Tensor& q, const at::Tensor& theta, const at::Tensor& eta,
+                           const at::Tensor& alpha);
 // comm.cu
 std::vector<at::Tensor> comm_alloc(int64_t nbytes, int64_t device);
 int64_t comm_ipc_open(const at::Tensor& handle, int64_t device);
@@ -90,6 +93,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_fwd_tc", &tb::attn_fwd_tc);
   m.def("attn_tc_supported", &tb::attn_tc_supported);
   m.def("attn_bwd_tc", &tb::attn_bwd_tc);
+  m.def("memory_scan_fwd", &tb::memory_scan_fwd);
   m.def("comm_alloc", &tb::comm_alloc);
   m.def("comm_ipc_open", &tb::comm_ipc_open);
   m.def("comm_ipc_close", &tb::comm_ipc_close);

@@ -72,7 +72,9 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 }
 
 // ---- activations (math written from the definitions) -------------------------
-__device__ __forceinline__ float sigmoidf_(float x) { return 1.f / (1.f + __expf(-x)); }
+// fast-division sigmoid: __fdividef returns 0 once the denominator overflows,
+// which is the correct limit for large negative x
+__device__ __forceinline__ float sigmoidf_(float x) { return __fdividef(1.f, 1.f + __expf(-x)); }
 __device__ __forceinline__ float silu_(float x) { return x * sigmoidf_(x); }
 __device__ __forceinline__ float silu_grad_(float x) {
   float s = sigmoidf_(x);

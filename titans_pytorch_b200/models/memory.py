@@ -12,7 +12,14 @@ including that ``set_weights`` writes the state into the parameters' storage
 (`memory.py:162-165`), so a MAC forward leaves the last chunk's memory in the
 parameters and the backward reads those values.  ``semantics="paper"`` is the
 paper's per-sample, per-head memory with per-token gates and a chunked update
-(see :mod:`titans_pytorch_b200.ops.memory_paper`).
+(:mod:`titans_pytorch_b200.ops.memory_paper`): ``memory_heads`` memories per
+sample, each initialised from the diagonal block of the shared ``MemoryMLP``
+weights (so the parameter layout is the reference's); per-token, per-head
+gates are the head means of the sigmoid gate projections, scaled by
+``memory_lr`` (theta), ``memory_momentum`` (eta) and ``memory_decay`` (alpha);
+states are ``[B, heads, out, in]``.  In paper mode the outer loss trains the
+query path and ``proj_out``; the memory state, keys, values and gates are
+learned at test time only.
 """
 
 from __future__ import annotations
@@ -27,6 +34,7 @@ from ..config import TitansConfig
 from ..ops.conv import conv_silu_norm
 from ..ops.memory import (activation_fn, memory_grads_reference, memory_step,
                           mlp_forward_reference)
+from ..ops.memory_paper import head_blocks, memory_scan, memory_scan_reference
 
 
 def get_activation(name: str) -> nn.Module:
@@ -89,6 +97,34 @@ class MemoryMLP(nn.Module):
 
     def compute_loss(self, keys: torch.Tensor, values: torch.Tensor) -> torch.Tensor:
         return F.mse_loss(self(keys), values, reduction="mean")
+
+
+class _PaperScan(torch.autograd.Function):
+    """Chunked paper-mode scan; differentiable in the queries only.
+
+    The memory state, keys, values and gates are test-time-learned (constants
+    for the outer loss).  The backward re-runs the scan to rebuild each chunk's
+    start weights and back-propagates the retrieval through them.
+    """
+
+    @staticmethod
+    def forward(ctx, q, k, v, theta, eta, alpha, chunk, act, use_kernels, nlayers, *state):
+        W, S = list(state[:nlayers]), list(state[nlayers:])
+        y, Wn, Sn = memory_scan(W, S, k, v, q.detach(), theta, eta, alpha, chunk, act, use_kernels)
+        ctx.save_for_backward(q, k, v, theta, eta, alpha, *state)
+        ctx.meta = (chunk, act, nlayers)
+        outs = [y.to(q.dtype)] + [w.detach() for w in Wn] + [m.detach() for m in Sn]
+        for t in outs[1:]:
+            ctx.mark_non_differentiable(t)
+        return tuple(outs)
+
+    @staticmethod
+    def backward(ctx, dy, *_):
+        q, k, v, theta, eta, alpha, *state = ctx.saved_tensors
+        chunk, act, nlayers = ctx.meta
+        _, _, _, dq = memory_scan_reference(state[:nlayers], state[nlayers:], k, v, q, theta, eta, alpha, chunk,
+                                            act, dy=dy)
+        return (dq.to(q.dtype),) + (None,) * (9 + len(state))
 
 
 class NeuralLongTermMemory(nn.Module):
@@ -169,13 +205,93 @@ class NeuralLongTermMemory(nn.Module):
             self.memory.requires_grad_(False)
         return g
 
+    # -------------------------------------------------------------- paper mode
+    @property
+    def paper(self) -> bool:
+        return self.config.semantics == "paper"
+
+    def _heads(self) -> tuple[int, int]:
+        h = self.config.memory_heads
+        return h, self.dim // h
+
+    def _split_heads(self, t: torch.Tensor) -> torch.Tensor:
+        """[B, T, D] -> [B*h, T, D/h]."""
+        B, T, _ = t.shape
+        h, dh = self._heads()
+        return t.reshape(B, T, h, dh).permute(0, 2, 1, 3).reshape(B * h, T, dh)
+
+    def _merge_heads(self, t: torch.Tensor, B: int) -> torch.Tensor:
+        h, dh = self._heads()
+        T = t.shape[1]
+        return t.reshape(B, h, T, dh).permute(0, 2, 1, 3).reshape(B, T, h * dh)
+
+    def _paper_inputs(self, x: torch.Tensor):
+        """Per-head unit queries (differentiable), keys, values and per-token gates."""
+        D = self.dim
+        h, dh = self._heads()
+        B, T, _ = x.shape
+        wq, bq = self._conv("conv_q")
+        q = conv_silu_norm(F.linear(x, self.proj_q.weight), wq, bq, False, self.use_kernels)
+        q = F.normalize(self._split_heads(q), dim=-1)
+        with torch.no_grad():
+            kv = F.linear(x, torch.cat([self.proj_k.weight, self.proj_v.weight], dim=0))
+            wk, bk = self._conv("conv_k")
+            wv, bv = self._conv("conv_v")
+            k = F.normalize(self._split_heads(conv_silu_norm(kv[..., :D], wk, bk, False, self.use_kernels)), dim=-1)
+            v = self._split_heads(conv_silu_norm(kv[..., D:], wv, bv, False, self.use_kernels))
+            gw, gb = self._gate_params()
+            g = torch.sigmoid(F.linear(x, torch.cat(gw, 0), torch.cat(gb, 0)).float())
+            g = g.view(B, T, 3, h, dh).mean(-1).permute(2, 0, 3, 1).reshape(3, B * h, T)
+            alpha = g[0] * self.config.memory_decay
+            theta = g[1] * self.config.memory_lr
+            eta = g[2] * self.config.memory_momentum
+        return q, k, v, theta.contiguous(), eta.contiguous(), alpha.contiguous()
+
+    def _paper_flat(self, state: MemoryState):
+        return ([w.reshape(-1, *w.shape[-2:]) for w in state.weights],
+                [m.reshape(-1, *m.shape[-2:]) for m in state.momentum])
+
+    def _paper_scan(self, x: torch.Tensor, state: MemoryState):
+        B = x.shape[0]
+        h, _ = self._heads()
+        q, k, v, theta, eta, alpha = self._paper_inputs(x)
+        W, S = self._paper_flat(state)
+        L = len(W)
+        outs = _PaperScan.apply(q, k, v, theta, eta, alpha, self.config.memory_chunk_size, self.config.activation,
+                                self.use_kernels, L, *W, *S)
+        y = self._merge_heads(outs[0], B)
+        shape = lambda t: t.reshape(B, h, *t.shape[-2:])  # noqa: E731
+        return y, MemoryState([shape(w) for w in outs[1:1 + L]], [shape(m) for m in outs[1 + L:]])
+
+    def _paper_retrieve(self, x: torch.Tensor, state: MemoryState) -> torch.Tensor:
+        B = x.shape[0]
+        q = self._paper_inputs(x)[0]
+        W, _ = self._paper_flat(state)
+        f = activation_fn(self.config.activation)
+        hcur = q.float()
+        for i, w in enumerate(W):
+            hcur = torch.bmm(hcur, w.float().transpose(1, 2))
+            if i < len(W) - 1:
+                hcur = f(hcur)
+        return self._merge_heads(hcur.to(x.dtype), B)
+
     # --------------------------------------------------------------------- API
-    def init_state(self, _batch_size: int = 1, _device=None) -> MemoryState:
+    def init_state(self, batch_size: int = 1, device=None) -> MemoryState:
+        if self.paper:
+            h, _ = self._heads()
+            w = [head_blocks(t.detach().float(), h) for t in self.memory.weight_list()]
+            w = [t.unsqueeze(0).expand(batch_size, *t.shape).clone() for t in w]
+            if device is not None:
+                w = [t.to(device) for t in w]
+            return MemoryState(weights=w, momentum=[torch.zeros_like(t) for t in w])
         w = self.memory.get_weights()
         return MemoryState(weights=w, momentum=[torch.zeros_like(t) for t in w])
 
     def _update(self, x: torch.Tensor, state: MemoryState) -> MemoryState:
         """New state after one update with the tokens of ``x`` (no retrieval output)."""
+        if self.paper:
+            with torch.no_grad():
+                return self._paper_scan(x.detach(), state)[1]
         k, v = self._keys_values(x)
         gw, gb = self._gate_params()
         new_w, new_m = memory_step(k, v, x.detach(), state.weights, state.momentum, gw, gb,
@@ -193,8 +309,12 @@ class NeuralLongTermMemory(nn.Module):
         """
         if state is None:
             state = self.init_state(x.shape[0], x.device)
-        else:
+        elif not self.paper:
             self.memory.set_weights(state.weights)
+        if self.paper:
+            y, new_state = self._paper_scan(x, state)
+            out = F.linear(y, self.proj_out.weight)
+            return (out, new_state) if return_state else (out, None)
         retrieved = self.memory(self._queries(x))
         new_state = self._update(x, state)
         out = F.linear(retrieved, self.proj_out.weight)
@@ -202,6 +322,8 @@ class NeuralLongTermMemory(nn.Module):
 
     def retrieve(self, queries: torch.Tensor, state: MemoryState) -> torch.Tensor:
         """proj_out(M(q)) with the memory set to ``state`` (no update)."""
+        if self.paper:
+            return F.linear(self._paper_retrieve(queries, state), self.proj_out.weight)
         self.memory.set_weights(state.weights)
         return F.linear(self.memory(self._queries(queries)), self.proj_out.weight)
 

@@ -7,7 +7,16 @@ micro-batch 8 per GPU; synthetic token ids uniform over [0, 32000), random
 init (std 0.02).  The memory update runs in the reference's semantics (one
 update per forward over the whole sequence), so "memory chunk" does not apply.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config NAME]
+
+``--config`` (default ``mag170m``, the headline) also selects the larger
+training workloads of the same metric: ``mac400m`` (TitansMAC, dim 1024, 24
+layers, 16 heads, segment 512, 16 persistent tokens, L_M=2; sequence 8192,
+micro-batch 4 per GPU) and ``mal760m`` (TitansMAL, dim 1536, 24 layers, 16
+heads of 96, window 1024, L_M=3; sequence 16384, micro-batch 1 per GPU, with
+activation checkpointing).  For N > 1 this framework runs its fused
+data-parallel engine (replicated weights, optimizer state sharded over the
+ranks) and the reference arm runs PyTorch FSDP2 ``fully_shard`` on those two.
 
 For N > 1 launch one process per GPU with torchrun (RANK/LOCAL_RANK/WORLD_SIZE
 from the environment).  Rank 0 prints one JSON line.
@@ -43,7 +52,29 @@ MODEL_FIELDS = dict(vocab_size=32000, dim=768, num_layers=12, num_heads=12, wind
                     num_persistent_tokens=4, conv_kernel_size=4, use_conv=True, use_rope=True,
                     dropout=0.0, max_seq_len=4096, init_std=0.02)
 SEQ, MICRO_BATCH = 4096, 8
+CONFIGS = {
+    "mag170m": dict(model="mag", fields=MODEL_FIELDS, seq=4096, micro_batch=8, ckpt=False,
+                    desc="TitansMAG ~170M ({p:.1f}M params; dim 768, 12 layers, 12 heads, window 512, L_M=2, "
+                         "4 persistent tokens, vocab 32000)"),
+    "mac400m": dict(model="mac", fields=dict(vocab_size=32000, dim=1024, num_layers=24, num_heads=16,
+                                             chunk_size=512, window_size=512, num_memory_layers=2,
+                                             memory_hidden_mult=4.0, ffn_mult=4.0, num_persistent_tokens=16,
+                                             conv_kernel_size=4, use_conv=True, use_rope=True, dropout=0.0,
+                                             max_seq_len=8192, init_std=0.02),
+                    seq=8192, micro_batch=4, ckpt=False,
+                    desc="TitansMAC ~400M ({p:.1f}M params; dim 1024, 24 layers, 16 heads, segment 512, "
+                         "16 persistent tokens, L_M=2, vocab 32000)"),
+    "mal760m": dict(model="mal", fields=dict(vocab_size=32000, dim=1536, num_layers=24, num_heads=16,
+                                             window_size=1024, chunk_size=1024, num_memory_layers=3,
+                                             memory_hidden_mult=4.0, ffn_mult=4.0, num_persistent_tokens=4,
+                                             conv_kernel_size=4, use_conv=True, use_rope=True, dropout=0.0,
+                                             max_seq_len=16384, init_std=0.02),
+                    seq=16384, micro_batch=1, ckpt=True,
+                    desc="TitansMAL ~760M ({p:.1f}M params; dim 1536, 24 layers, 16 heads of 96, window 1024, "
+                         "L_M=3, vocab 32000; activation checkpointing)"),
+}
 LR, BETAS, WD, CLIP = 4e-4, (0.9, 0.95), 0.1, 1.0
+CFG = None
 
 
 # ---------------------------------------------------------------------------- helpers
@@ -174,17 +205,23 @@ def count_launches(step_fn, prefixes) -> tuple[int, int]:
 
 # ---------------------------------------------------------------------------- arms
 def build_ours(device, world):
-    from titans_pytorch_b200 import TitansConfig, TitansMAG
+    from titans_pytorch_b200 import TitansConfig, create_model
     from titans_pytorch_b200.train.trainer import Trainer, TrainStepConfig
+    from titans_pytorch_b200.utils.perf import enable_gradient_checkpointing
 
     torch.manual_seed(0)
-    model = TitansMAG(TitansConfig(**MODEL_FIELDS))
+    model = create_model(CFG["model"], TitansConfig(**MODEL_FIELDS))
+    if CFG["ckpt"]:
+        enable_gradient_checkpointing(model)
     engine = None
     if world > 1:
         from titans_pytorch_b200.parallel.ddp import DataParallelEngine
 
         engine = DataParallelEngine()
-    tr = Trainer(model, TrainStepConfig(lr=LR, betas=BETAS, weight_decay=WD, grad_clip=CLIP),
+    # one GPU: the whole step is captured in a CUDA graph (two eager warm-up
+    # steps, the capture on the third warm-up call, replays in the timed region)
+    tr = Trainer(model, TrainStepConfig(lr=LR, betas=BETAS, weight_decay=WD, grad_clip=CLIP,
+                                        cuda_graph=world == 1, graph_warmup=2),
                  device=device, engine=engine)
     nparams = sum(p.numel() for p in tr.optimizer.space.params)
     return tr, nparams
@@ -198,12 +235,24 @@ def build_reference(device, world, local):
     import titans  # the reference package, unmodified
 
     torch.manual_seed(0)
-    model = titans.TitansMAG(titans.TitansConfig(**MODEL_FIELDS))
+    cls = {"mag": titans.TitansMAG, "mac": titans.TitansMAC, "mal": titans.TitansMAL}[CFG["model"]]
+    model = cls(titans.TitansConfig(**MODEL_FIELDS))
     # the reference trainer's bf16 mode: the whole model in bf16 (scripts/pretrain.py:460-463)
     model = model.to(device=device, dtype=torch.bfloat16)
     nparams = sum(p.numel() for p in model.parameters())
+    # No activation checkpointing on this arm: the reference's own
+    # enable_gradient_checkpointing (optimized_training.py:428-457) fails in the
+    # recompute (its memory update runs torch.autograd.grad inside the
+    # checkpointed block, so the recomputed graph differs); without it the arm
+    # only skips recomputation.
     wrapped = model
-    if world > 1:
+    if world > 1 and CFG["model"] != "mag":
+        from torch.distributed.fsdp import fully_shard
+
+        for blk in model.blocks:
+            fully_shard(blk)
+        fully_shard(model)
+    elif world > 1:
         from torch.nn.parallel import DistributedDataParallel as DDP
 
         # find_unused_parameters=True: the memory gates / key-value projections never get
@@ -237,7 +286,11 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="mag170m")
     args = ap.parse_args()
+    global CFG, MODEL_FIELDS, SEQ, MICRO_BATCH
+    CFG = CONFIGS[args.config]
+    MODEL_FIELDS, SEQ, MICRO_BATCH = CFG["fields"], CFG["seq"], CFG["micro_batch"]
     world, rank, local = dist_env()
     if world != args.gpus:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}; launch with torchrun for N>1")
@@ -310,22 +363,27 @@ def main():
 
     tokens = world * MICRO_BATCH * SEQ
     value = tokens / (ms / 1000)
+    parallelism = f"dp{world}"
+    if world > 1 and CFG["model"] != "mag":
+        parallelism = f"fsdp{world}" if args.impl == "reference" else f"dp{world} (optimizer state sharded)"
     if rank == 0:
         out = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": W,
             "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "bf16", "data": "synthetic uniform token ids, random init (std 0.02)",
-            "config": {"model": f"TitansMAG ~170M ({nparams / 1e6:.1f}M params; dim 768, 12 layers, 12 heads, "
-                                "window 512, L_M=2, 4 persistent tokens, vocab 32000)",
-                       "global_batch": MICRO_BATCH * world, "seq_len": SEQ, "parallelism": f"dp{world}",
-                       "l2": "no flush: per-step working set (0.49 GB weights + activations) >> 126 MB L2"},
+            "config": {"model": CFG["desc"].format(p=nparams / 1e6),
+                       "global_batch": MICRO_BATCH * world, "seq_len": SEQ, "parallelism": parallelism,
+                       "l2": "no flush: per-step working set (weights + activations, several GB) >> 126 MB L2"},
             "clocks": clocks, "e2e": e2e, "gpu_launches": ours * K, "all_launches_per_step": total,
             "final_loss": final_loss,
         }
         if args.impl == "reference":
             out["impl"] = "reference"
             out["reference_mode"] = ("as shipped: unmodified package, bf16 model (scripts/pretrain.py:460), "
-                                     "fused AdamW, clip 1.0; DDP find_unused_parameters=True for N>1")
+                                     "fused AdamW, clip 1.0; DDP find_unused_parameters=True for N>1 "
+                                     "(FSDP2 fully_shard per block for the MAC/MAL configs)"
+                                     + ("; activation checkpointing off (the reference's own "
+                                        "enable_gradient_checkpointing fails in its recompute)" if CFG["ckpt"] else ""))
         else:
             out["impl"] = "ours"
         print(json.dumps(out))

@@ -84,3 +84,27 @@ def test_reference_weights_logit_parity_bf16():
     with torch.no_grad():
         ol, _ = om(ids.cuda())
     assert float((ol.float().cpu() - rl).abs().max()) < 1e-2
+
+
+@pytest.mark.parametrize("kind", ["mag", "mac"])
+def test_cuda_graph_training_matches_eager(kind):
+    """Graph-captured training steps (device-side step count and LR schedule) equal eager steps."""
+    from titans_pytorch_b200.train.trainer import Trainer, TrainStepConfig
+
+    cfg = T.TitansConfig(dim=128, num_heads=2, num_layers=2, vocab_size=512, chunk_size=64, window_size=32,
+                         num_persistent_tokens=4, dropout=0.0, max_seq_len=256)
+    torch.manual_seed(0)
+    a = T.create_model(kind, cfg)
+    b = T.create_model(kind, cfg)
+    b.load_state_dict(a.state_dict())
+    sc = dict(lr=1e-3, warmup_steps=3, total_steps=10)
+    ta = Trainer(a, TrainStepConfig(**sc), device="cuda")
+    tb_ = Trainer(b, TrainStepConfig(**sc, cuda_graph=True, graph_warmup=2), device="cuda")
+    g = torch.Generator().manual_seed(1)
+    for step in range(7):
+        ids = torch.randint(0, 512, (2, 129), generator=g)
+        batch = {"input_ids": ids[:, :-1].cuda(), "labels": ids[:, 1:].cuda()}
+        la, lb = float(ta.train_step(batch)), float(tb_.train_step(batch))
+        assert abs(la - lb) <= 2e-3 * abs(la), (step, la, lb)
+    for pa, pb in zip(ta.model.parameters(), tb_.model.parameters()):
+        torch.testing.assert_close(pa.float(), pb.float(), atol=2e-2, rtol=2e-2)

@@ -34,7 +34,9 @@ at::Tensor grad_norm_clip(const at::Tensor& grads, const at::Tensor& tab, int64_
 void adamw_step(at::Tensor& master, at::Tensor& exp_avg, at::Tensor& exp_avg_sq, const at::Tensor& grads,
                 const c10::optional<at::Tensor>& params_out, const at::Tensor& tab, int64_t nseg, int64_t items,
                 const c10::optional<at::Tensor>& clip, double gscale, double lr, double beta1, double beta2,
-                double eps, double wd, int64_t step);
+                double eps, double wd, int64_t step, const c10::optional<at::Tensor>& hyper);
+void adamw_hyper_step(at::Tensor& hyper, double base_lr, double beta1, double beta2, int64_t warmup, int64_t total,
+                      double min_ratio, bool use_schedule);
 // attention.cu
 std::vector<at::Tensor> attn_pack(const at::Tensor& qkv, const c10::optional<at::Tensor>& pkv, int64_t H,
                                   const c10::optional<at::Tensor>& inv_freq);
@@ -85,7 +87,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("cross_entropy_fwd", &tb::cross_entropy_fwd);
   m.def("cross_entropy_bwd", &tb::cross_entropy_bwd);
   m.def("grad_norm_clip", &tb::grad_norm_clip);
-  m.def("adamw_step", &tb::adamw_step);
+  m.def("adamw_step", &tb::adamw_step, pybind11::arg("master"), pybind11::arg("exp_avg"), pybind11::arg("exp_avg_sq"),
+        pybind11::arg("grads"), pybind11::arg("params_out"), pybind11::arg("tab"), pybind11::arg("nseg"),
+        pybind11::arg("items"), pybind11::arg("clip"), pybind11::arg("gscale"), pybind11::arg("lr"),
+        pybind11::arg("beta1"), pybind11::arg("beta2"), pybind11::arg("eps"), pybind11::arg("wd"),
+        pybind11::arg("step"), pybind11::arg("hyper") = pybind11::none());
+  m.def("adamw_hyper_step", &tb::adamw_hyper_step);
   m.def("attn_pack", &tb::attn_pack);
   m.def("attn_fwd_packed", &tb::attn_fwd_packed);
   m.def("attn_bwd_packed", &tb::attn_bwd_packed);

@@ -62,7 +62,12 @@ __global__ void adamw_kernel(float* __restrict__ master, float* __restrict__ m, 
                              const G* __restrict__ g, P* __restrict__ pout, const int64_t* __restrict__ segs,
                              const int64_t* __restrict__ item_start, int nseg, int64_t nitems,
                              const float* __restrict__ clip, float gscale, float lr, float b1, float b2, float eps,
-                             float wd, float bc1, float bc2_sqrt) {
+                             float wd, float bc1, float bc2_sqrt, const float* __restrict__ hyper) {
+  if (hyper) {  // step-dependent values from the device (CUDA-graph replay)
+    lr = hyper[1];
+    bc1 = hyper[2];
+    bc2_sqrt = hyper[3];
+  }
   const float cg = gscale * (clip ? clip[1] : 1.f);
   const float step = lr / bc1;
   const float decay = 1.f - lr * wd;
@@ -83,6 +88,38 @@ __global__ void adamw_kernel(float* __restrict__ master, float* __restrict__ m, 
       if (pout) pout[i] = from_f<P>(p);
     }
   }
+}
+
+// hyper = [step, lr, 1 - b1^step, sqrt(1 - b2^step)] (fp32, device): advance
+// the step and recompute the rest, with the learning-rate multiplier of a
+// linear warm-up then cosine decay to min_ratio (applied to step - 1, as a
+// scheduler stepped after each update does), or 1 without a schedule.
+__global__ void adamw_hyper_kernel(float* __restrict__ hyper, float base_lr, float b1, float b2, int warmup,
+                                   int total, float min_ratio, int use_schedule) {
+  const float step = hyper[0] + 1.f;
+  hyper[0] = step;
+  float mult = 1.f;
+  if (use_schedule) {
+    const float k = step - 1.f;
+    if (k < (float)warmup) {
+      mult = k / (float)max(1, warmup);
+    } else {
+      const float progress = (k - (float)warmup) / (float)max(1, total - warmup);
+      mult = fmaxf(min_ratio, 0.5f * (1.f + cosf(3.14159265358979f * progress)));
+    }
+  }
+  hyper[1] = base_lr * mult;
+  hyper[2] = 1.f - powf(b1, step);
+  hyper[3] = sqrtf(1.f - powf(b2, step));
+}
+
+void adamw_hyper_step(at::Tensor& hyper, double base_lr, double beta1, double beta2, int64_t warmup, int64_t total,
+                      double min_ratio, bool use_schedule) {
+  TORCH_CHECK(hyper.is_cuda() && hyper.scalar_type() == at::kFloat && hyper.numel() == 4, "adamw_hyper: float[4]");
+  const at::cuda::CUDAGuard guard(hyper.device());
+  adamw_hyper_kernel<<<1, 1, 0, stream()>>>(hyper.data_ptr<float>(), (float)base_lr, (float)beta1, (float)beta2,
+                                            (int)warmup, (int)total, (float)min_ratio, use_schedule ? 1 : 0);
+  check_launch("adamw_hyper_step");
 }
 
 // `tab` (device int64): [off0, len0, off1, len1, ..., item_start0, item_start1, ...]
@@ -116,7 +153,7 @@ at::Tensor grad_norm_clip(const at::Tensor& grads, const at::Tensor& tab, int64_
 void adamw_step(at::Tensor& master, at::Tensor& exp_avg, at::Tensor& exp_avg_sq, const at::Tensor& grads,
                 const c10::optional<at::Tensor>& params_out, const at::Tensor& tab, int64_t nseg, int64_t items,
                 const c10::optional<at::Tensor>& clip, double gscale, double lr, double beta1, double beta2,
-                double eps, double wd, int64_t step) {
+                double eps, double wd, int64_t step, const c10::optional<at::Tensor>& hyper) {
   const at::cuda::CUDAGuard guard(master.device());
   TORCH_CHECK(master.scalar_type() == at::kFloat && exp_avg.scalar_type() == at::kFloat &&
                   exp_avg_sq.scalar_type() == at::kFloat, "adamw: fp32 master/state");
@@ -136,7 +173,8 @@ void adamw_step(at::Tensor& master, at::Tensor& exp_avg, at::Tensor& exp_avg_sq,
     adamw_kernel<G, P><<<blocks, 512, 0, stream()>>>(
         master.data_ptr<float>(), exp_avg.data_ptr<float>(), exp_avg_sq.data_ptr<float>(), (const G*)grads.data_ptr(),
         has_out ? (P*)params_out->data_ptr() : nullptr, segs, istart, nseg, items, cl, (float)gscale, (float)lr,
-        (float)beta1, (float)beta2, (float)eps, (float)wd, bc1, bc2s);
+        (float)beta1, (float)beta2, (float)eps, (float)wd, bc1, bc2s,
+        (hyper.has_value() && hyper->defined()) ? hyper->data_ptr<float>() : nullptr);
   };
   const bool gb = grads.scalar_type() == at::kBFloat16;
   const bool pb = !has_out || params_out->scalar_type() == at::kBFloat16;

@@ -163,8 +163,17 @@ class FusedAdamW(torch.optim.Optimizer):
         """Multiplier applied to the raw flat gradient (1 here; 1/world in DP)."""
         return 1.0
 
+    def make_hyper(self) -> torch.Tensor:
+        """Device copy of the step-dependent values for CUDA-graph replay:
+        ``[step, lr, 1 - b1^step, sqrt(1 - b2^step)]``, starting at this step."""
+        return torch.tensor([float(self.step_count), 0.0, 0.0, 0.0], dtype=torch.float32, device=self.space.device)
+
     @torch.no_grad()
-    def step(self, closure=None):
+    def step(self, closure=None, hyper: torch.Tensor | None = None, schedule: tuple | None = None):
+        """One update.  With ``hyper`` (see :meth:`make_hyper`) the step count,
+        learning rate and bias corrections are advanced and read on the device
+        (``schedule`` = (warmup, total, min_ratio) or None), so the launch
+        sequence is identical every step and can be replayed from a CUDA graph."""
         loss = closure() if closure is not None else None
         g = self.param_groups[0]
         lr, (b1, b2), eps, wd = g["lr"], g["betas"], g["eps"], g["weight_decay"]
@@ -179,8 +188,12 @@ class FusedAdamW(torch.optim.Optimizer):
                 clip = E.grad_norm_clip(s.grad, tab, nseg, items, gs, self.max_grad_norm)
                 self.last_grad_norm = clip[0]
             out = None if self.master is s.flat else s.flat
+            if hyper is not None:
+                base = g.get("initial_lr", lr)
+                warm, total, mr = schedule if schedule is not None else (0, 1, 1.0)
+                E.adamw_hyper_step(hyper, base, b1, b2, warm, total, mr, schedule is not None)
             E.adamw_step(self.master, self.exp_avg, self.exp_avg_sq, s.grad, out, tab, nseg, items,
-                         clip, gs, lr, b1, b2, eps, wd, self.step_count)
+                         clip, gs, lr, b1, b2, eps, wd, self.step_count, hyper)
         else:
             self._step_reference(lr, b1, b2, eps, wd, gs)
         return loss

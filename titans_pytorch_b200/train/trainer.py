@@ -46,6 +46,10 @@ class TrainStepConfig:
     min_lr_ratio: float = 0.1
     gradient_accumulation_steps: int = 1
     dtype: torch.dtype = torch.bfloat16
+    # Capture the whole step (forward, backward, clip, AdamW, zero-grad) in a
+    # CUDA graph after `graph_warmup` eager steps and replay it afterwards.
+    cuda_graph: bool = False
+    graph_warmup: int = 3
 
 
 class Trainer:
@@ -73,6 +77,13 @@ class Trainer:
         self.global_step = 0
         self._micro = 0
         self.optimizer.zero_grad()
+        self._graph = None
+        self._eager_graph_steps = 0
+        if self.cfg.cuda_graph:
+            if self.device.type != "cuda" or engine is not None or self.cfg.gradient_accumulation_steps != 1:
+                raise ValueError("cuda_graph needs one CUDA device, no data-parallel engine and no accumulation")
+            if not getattr(self.optimizer, "kernels", False):
+                raise ValueError("cuda_graph needs the fused optimizer kernels")
 
     def _to_device(self, t: torch.Tensor) -> torch.Tensor:
         return t.to(self.device, non_blocking=True)
@@ -88,6 +99,8 @@ class Trainer:
         Returns the micro-batch loss as a device tensor (no host sync).
         """
         self.model.train()
+        if self.cfg.cuda_graph:
+            return self._graph_step(batch)
         ids = self._to_device(batch["input_ids"])
         labels = self._to_device(batch["labels"])
         accum = self.cfg.gradient_accumulation_steps
@@ -97,6 +110,60 @@ class Trainer:
         if self._micro % accum == 0:
             self.optimizer_step()
         return loss.detach()
+
+    # ------------------------------------------------------------ CUDA graph
+    def _schedule(self):
+        if self.scheduler is None:
+            return None
+        return (self.cfg.warmup_steps, max(self.cfg.total_steps, 1), self.cfg.min_lr_ratio)
+
+    def _graph_step(self, batch) -> torch.Tensor:
+        """Eager warm-up steps on a side stream, then one capture, then replays.
+
+        Every replay runs the same kernels on the same buffers: the batch is
+        copied into static input tensors, and the step count, learning rate and
+        bias corrections live on the device (see ``FusedAdamW.step``).
+        """
+        cur = torch.cuda.current_stream(self.device)
+        if self._graph is None and self._eager_graph_steps < self.cfg.graph_warmup:
+            side = torch.cuda.Stream(self.device)
+            side.wait_stream(cur)
+            with torch.cuda.stream(side):
+                ids = self._to_device(batch["input_ids"])
+                labels = self._to_device(batch["labels"])
+                loss = self.loss_fn(ids, labels)
+                loss.backward()
+                self.optimizer_step()
+            cur.wait_stream(side)
+            self._eager_graph_steps += 1
+            return loss.detach()
+        if self._graph is None:
+            self._capture(batch)
+        self._static_ids.copy_(batch["input_ids"], non_blocking=True)
+        self._static_labels.copy_(batch["labels"], non_blocking=True)
+        self._graph.replay()
+        self.optimizer.step_count += 1
+        self.global_step += 1
+        return self._static_loss
+
+    def _capture(self, batch) -> None:
+        self._static_ids = batch["input_ids"].to(self.device).clone()
+        self._static_labels = batch["labels"].to(self.device).clone()
+        self._hyper = self.optimizer.make_hyper()
+        sched = self._schedule()
+        opt = self.optimizer
+        opt.zero_grad()
+        torch.cuda.synchronize(self.device)
+        g = torch.cuda.CUDAGraph()
+        saved_count = opt.step_count
+        with torch.cuda.graph(g):
+            loss = self.loss_fn(self._static_ids, self._static_labels)
+            loss.backward()
+            opt.step(hyper=self._hyper, schedule=sched)
+            opt.zero_grad()
+            self._static_loss = loss.detach()
+        opt.step_count = saved_count  # capture recorded the work without running it
+        self._graph = g
 
     def optimizer_step(self) -> None:
         if self.engine is not None:

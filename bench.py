@@ -16,7 +16,9 @@ micro-batch 4 per GPU) and ``mal760m`` (TitansMAL, dim 1536, 24 layers, 16
 heads of 96, window 1024, L_M=3; sequence 16384, micro-batch 1 per GPU, with
 activation checkpointing).  For N > 1 this framework runs its fused
 data-parallel engine (replicated weights, optimizer state sharded over the
-ranks) and the reference arm runs PyTorch FSDP2 ``fully_shard`` on those two.
+ranks); the reference arm averages gradients with one NCCL all-reduce after
+backward (its own DDP setting raises, and DDP with unused-parameter search
+stalls).
 
 For N > 1 launch one process per GPU with torchrun (RANK/LOCAL_RANK/WORLD_SIZE
 from the environment).  Rank 0 prints one JSON line.
@@ -93,7 +95,7 @@ def init_dist(world, local):
         import torch.distributed as dist
 
         os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
 
 
@@ -218,10 +220,11 @@ def build_ours(device, world):
         from titans_pytorch_b200.parallel.ddp import DataParallelEngine
 
         engine = DataParallelEngine()
-    # one GPU: the whole step is captured in a CUDA graph (two eager warm-up
-    # steps, the capture on the third warm-up call, replays in the timed region)
+    # the whole step (with the fused data-parallel reduce/update for N > 1) is
+    # captured in a CUDA graph: two eager warm-up steps, the capture on the third
+    # warm-up call, replays in the timed region
     tr = Trainer(model, TrainStepConfig(lr=LR, betas=BETAS, weight_decay=WD, grad_clip=CLIP,
-                                        cuda_graph=world == 1, graph_warmup=2),
+                                        cuda_graph=True, graph_warmup=2),
                  device=device, engine=engine)
     nparams = sum(p.numel() for p in tr.optimizer.space.params)
     return tr, nparams
@@ -245,24 +248,29 @@ def build_reference(device, world, local):
     # recompute (its memory update runs torch.autograd.grad inside the
     # checkpointed block, so the recomputed graph differs); without it the arm
     # only skips recomputation.
-    wrapped = model
-    if world > 1 and CFG["model"] != "mag":
-        from torch.distributed.fsdp import fully_shard
+    # Data parallel for N > 1: gradients averaged with one flat NCCL all-reduce
+    # after backward.  The reference's own DDP setting (find_unused_parameters=
+    # False) raises at the second iteration, and DDP with find_unused_parameters=
+    # True stalls in an all-reduce (its memory update calls torch.autograd.grad
+    # inside the forward); FSDP would shard the parameters its memory update
+    # rewrites through .data.
+    params = [p for p in model.parameters() if p.requires_grad]
 
-        for blk in model.blocks:
-            fully_shard(blk)
-        fully_shard(model)
-    elif world > 1:
-        from torch.nn.parallel import DistributedDataParallel as DDP
+    def allreduce_grads():
+        import torch.distributed as dist
 
-        # find_unused_parameters=True: the memory gates / key-value projections never get
-        # gradients, and the reference's own DDP setting raises at the 2nd iteration.
-        wrapped = DDP(model, device_ids=[local], find_unused_parameters=True)
+        grads = [p.grad for p in params if p.grad is not None]
+        flat = torch._utils._flatten_dense_tensors(grads)
+        dist.all_reduce(flat)
+        flat.div_(world)
+        for g, f in zip(grads, torch._utils._unflatten_dense_tensors(flat, grads)):
+            g.copy_(f)
+
     opt = torch.optim.AdamW(model.parameters(), lr=LR, betas=BETAS, weight_decay=WD, fused=True)
 
     class RefStep:
         def __init__(self):
-            self.model, self.opt = wrapped, opt
+            self.model, self.opt = model, opt
 
         def train_step(self, batch):
             ids = batch["input_ids"].to(device, non_blocking=True)
@@ -270,6 +278,8 @@ def build_reference(device, world, local):
             logits, _ = self.model(ids)
             loss = torch.nn.functional.cross_entropy(logits.view(-1, logits.size(-1)), lab.view(-1))
             loss.backward()
+            if world > 1:
+                allreduce_grads()
             torch.nn.utils.clip_grad_norm_(model.parameters(), CLIP)
             self.opt.step()
             self.opt.zero_grad(set_to_none=True)
@@ -358,14 +368,16 @@ def main():
         e2e = {"value": tok / (ems / 1000), "unit": "tokens/s", "ms_per_step": ems, "wall_ms_per_step": wall,
                "h2d_bytes_per_step": bi, "d2h_bytes_per_step": 4}
 
-    # launch count of one extra (untimed) step
-    ours, total = count_launches(lambda: trainer.train_step(dev_batches[-1]), prefixes) if rank == 0 else (0, 0)
+    # launch count of one extra (untimed) step; every rank takes it, so the ranks'
+    # collectives stay matched
+    ours, total = count_launches(lambda: trainer.train_step(dev_batches[-1]), prefixes)
 
     tokens = world * MICRO_BATCH * SEQ
     value = tokens / (ms / 1000)
     parallelism = f"dp{world}"
-    if world > 1 and CFG["model"] != "mag":
-        parallelism = f"fsdp{world}" if args.impl == "reference" else f"dp{world} (optimizer state sharded)"
+    if world > 1:
+        parallelism = (f"dp{world} (grads all-reduced after backward)" if args.impl == "reference"
+                       else f"dp{world} (fused reduce-scatter / AdamW shard / all-gather)")
     if rank == 0:
         out = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": W,
@@ -380,8 +392,8 @@ def main():
         if args.impl == "reference":
             out["impl"] = "reference"
             out["reference_mode"] = ("as shipped: unmodified package, bf16 model (scripts/pretrain.py:460), "
-                                     "fused AdamW, clip 1.0; DDP find_unused_parameters=True for N>1 "
-                                     "(FSDP2 fully_shard per block for the MAC/MAL configs)"
+                                     "fused AdamW, clip 1.0; for N>1 grads averaged by one flat NCCL all-reduce "
+                                     "after backward (its DDP raises or stalls)"
                                      + ("; activation checkpointing off (the reference's own "
                                         "enable_gradient_checkpointing fails in its recompute)" if CFG["ckpt"] else ""))
         else:
@@ -390,6 +402,8 @@ def main():
     if world > 1:
         import torch.distributed as dist
 
+        if hasattr(trainer, "_graph"):
+            trainer._graph = None  # release the captured step before the group goes away
         dist.destroy_process_group()
 
 

@@ -100,7 +100,7 @@ def test_data_parallel_collective_matches_single_process(tmp_path):
 
 
 # ------------------------------------------------------------------ GPUs
-def _fused_worker(rank, world, out_dir, steps):
+def _fused_worker(rank, world, out_dir, steps, graph=False):
     import datetime
 
     from titans_pytorch_b200.parallel.ddp import DataParallelEngine
@@ -111,23 +111,28 @@ def _fused_worker(rank, world, out_dir, steps):
     torch.manual_seed(0)
     model = T.TitansMAG(T.TitansConfig(**FIELDS))
     eng = DataParallelEngine(reduce="fused")
-    tr = Trainer(model, TrainStepConfig(lr=1e-3), device=f"cuda:{rank}", engine=eng)
+    tr = Trainer(model, TrainStepConfig(lr=1e-3, cuda_graph=graph, graph_warmup=2), device=f"cuda:{rank}",
+                 engine=eng)
     for b in _batches(steps, 2, 64, seed=1):  # every rank sees the same batch
-        tr.train_step(b)
+        tr.train_step({k: v.to(f"cuda:{rank}") for k, v in b.items()})
     torch.cuda.synchronize()
     tr.optimizer.check_errors()
     flat = tr.optimizer.space.flat.float().cpu()
     torch.save(flat, os.path.join(out_dir, f"fused_{rank}.pt"))
+    tr._graph = None  # release the captured step before the group goes away
     tr.optimizer.close()
     dist.destroy_process_group()
 
 
 @pytest.mark.gpu
-def test_data_parallel_fused_matches_single_gpu(tmp_path):
+@pytest.mark.parametrize("graph", [False, True])
+def test_data_parallel_fused_matches_single_gpu(tmp_path, graph):
+    """2 ranks, fused peer-memory step (eager, or captured in a CUDA graph after two
+    eager steps and replayed) against one GPU on the same batches."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
-    steps = 3
-    run_workers(_fused_worker, 2, (str(tmp_path), steps), timeout=240)
+    steps = 5 if graph else 3
+    run_workers(_fused_worker, 2, (str(tmp_path), steps, graph), timeout=240)
     f0 = torch.load(tmp_path / "fused_0.pt")
     f1 = torch.load(tmp_path / "fused_1.pt")
     assert torch.equal(f0, f1), "ranks hold different weights after the fused step"

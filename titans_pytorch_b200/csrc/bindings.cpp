@@ -62,13 +62,15 @@ at::Tensor memory_scan_fwd(at::Tensor& W1, at::Tensor& S1, at::Tensor& W2T, at::
 std::vector<at::Tensor> comm_alloc(int64_t nbytes, int64_t device);
 int64_t comm_ipc_open(const at::Tensor& handle, int64_t device);
 void comm_ipc_close(int64_t ptr);
-void comm_barrier(const at::Tensor& sig_ptrs, int64_t slot, int64_t epoch, int64_t world, int64_t me, at::Tensor& err);
+void comm_barrier(const at::Tensor& sig_ptrs, int64_t slot, at::Tensor& epoch, bool bump, int64_t world, int64_t me,
+                  at::Tensor& err);
 void comm_reduce_shard(const at::Tensor& grad_ptrs, int64_t lo, int64_t n, at::Tensor& gsum, double gscale,
                        const at::Tensor& slot_ptrs, int64_t world, int64_t me);
 void comm_adamw_shard(const at::Tensor& gsum, at::Tensor& master, at::Tensor& exp_avg, at::Tensor& exp_avg_sq,
                       const at::Tensor& param_ptrs, int64_t lo, int64_t world, const at::Tensor& tab, int64_t nseg,
                       int64_t items, const at::Tensor& norm_slots, double gscale, double max_norm, double lr,
-                      double beta1, double beta2, double eps, double wd, int64_t step, at::Tensor& norm_out);
+                      double beta1, double beta2, double eps, double wd, int64_t step, at::Tensor& norm_out,
+                      const c10::optional<at::Tensor>& hyper);
 }  // namespace tb
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {

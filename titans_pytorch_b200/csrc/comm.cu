@@ -16,7 +16,9 @@
 //   barrier 2        every rank's P is complete before the next forward
 // Barriers are epoch counters: rank s stores the epoch into sig[k][s] of every
 // peer (release, system scope) and waits until its own sig[k][*] reach the
-// epoch (acquire).  Every wait is bounded (~2^31 cycles); a timeout sets an
+// epoch (acquire).  The epoch lives in a device word that the step's first
+// barrier advances, so the step's launches are identical every step (CUDA-graph
+// replay).  Every wait is bounded (~2^31 cycles); a timeout sets an
 // error word and the kernel returns.  No multicast / NVLS is used.
 #include "common.cuh"
 
@@ -34,10 +36,18 @@ __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;\n" ::"l"(p), "r"(v) : "memory");
 }
 
-// one block of `world` (>= 32 rounded) threads
-__global__ void barrier_kernel(uint32_t* const* __restrict__ sig_ptrs, int slot, uint32_t epoch, int world, int me,
-                               unsigned* __restrict__ err) {
+// one block of `world` (>= 32 rounded) threads; epoch = *epoch_dev (+1, stored
+// back, when `bump`)
+__global__ void barrier_kernel(uint32_t* const* __restrict__ sig_ptrs, int slot, uint32_t* __restrict__ epoch_dev,
+                               int bump, int world, int me, unsigned* __restrict__ err) {
   const int t = threadIdx.x;
+  __shared__ uint32_t ep;
+  if (t == 0) {
+    ep = *epoch_dev + (bump ? 1u : 0u);
+    if (bump) *epoch_dev = ep;
+  }
+  __syncthreads();
+  const uint32_t epoch = ep;
   __threadfence_system();  // everything this rank wrote before the barrier is visible system-wide
   if (t < world) st_release_sys(sig_ptrs[t] + slot * world + me, epoch);
   if (t < world) {
@@ -113,7 +123,12 @@ __global__ void adamw_shard_kernel(const float* __restrict__ gsum, float* __rest
                                    int world, const int64_t* __restrict__ segs, const int64_t* __restrict__ item_start,
                                    int nseg, int64_t nitems, const float* __restrict__ norm_slots, float gscale,
                                    float max_norm, float lr, float b1, float b2, float eps, float wd, float bc1,
-                                   float bc2_sqrt, float* __restrict__ norm_out) {
+                                   float bc2_sqrt, float* __restrict__ norm_out, const float* __restrict__ hyper) {
+  if (hyper) {  // [step, lr, bc1, sqrt(bc2)] advanced on the device (CUDA-graph replay)
+    lr = hyper[1];
+    bc1 = hyper[2];
+    bc2_sqrt = hyper[3];
+  }
   float tot = 0.f;
   for (int r = 0; r < world; ++r) tot += norm_slots[r];
   const float nrm = sqrtf(tot);
@@ -187,11 +202,13 @@ void comm_ipc_close(int64_t ptr) {
   if (ptr) C10_CUDA_CHECK(cudaIpcCloseMemHandle((void*)(uintptr_t)ptr));
 }
 
-void comm_barrier(const at::Tensor& sig_ptrs, int64_t slot, int64_t epoch, int64_t world, int64_t me,
+void comm_barrier(const at::Tensor& sig_ptrs, int64_t slot, at::Tensor& epoch, bool bump, int64_t world, int64_t me,
                   at::Tensor& err) {
+  TORCH_CHECK(epoch.is_cuda() && epoch.scalar_type() == at::kInt && epoch.numel() == 1, "comm_barrier: epoch word");
   comm::barrier_kernel<<<1, 32 * ((world + 31) / 32), 0, stream()>>>(
-      reinterpret_cast<uint32_t* const*>(sig_ptrs.data_ptr<int64_t>()), (int)slot, (uint32_t)epoch, (int)world,
-      (int)me, (unsigned*)err.data_ptr<int>());
+      reinterpret_cast<uint32_t* const*>(sig_ptrs.data_ptr<int64_t>()), (int)slot,
+      reinterpret_cast<uint32_t*>(epoch.data_ptr<int>()), bump ? 1 : 0, (int)world, (int)me,
+      (unsigned*)err.data_ptr<int>());
   check_launch("comm_barrier");
 }
 
@@ -214,7 +231,8 @@ void comm_reduce_shard(const at::Tensor& grad_ptrs, int64_t lo, int64_t n, at::T
 void comm_adamw_shard(const at::Tensor& gsum, at::Tensor& master, at::Tensor& exp_avg, at::Tensor& exp_avg_sq,
                       const at::Tensor& param_ptrs, int64_t lo, int64_t world, const at::Tensor& tab, int64_t nseg,
                       int64_t items, const at::Tensor& norm_slots, double gscale, double max_norm, double lr,
-                      double beta1, double beta2, double eps, double wd, int64_t step, at::Tensor& norm_out) {
+                      double beta1, double beta2, double eps, double wd, int64_t step, at::Tensor& norm_out,
+                      const c10::optional<at::Tensor>& hyper) {
   if (nseg == 0) return;
   const int64_t* segs = tab.data_ptr<int64_t>();
   const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>(items, num_sms() * 8));
@@ -224,7 +242,8 @@ void comm_adamw_shard(const at::Tensor& gsum, at::Tensor& master, at::Tensor& ex
       gsum.data_ptr<float>(), master.data_ptr<float>(), exp_avg.data_ptr<float>(), exp_avg_sq.data_ptr<float>(),
       reinterpret_cast<__nv_bfloat16* const*>(param_ptrs.data_ptr<int64_t>()), lo, (int)world, segs,
       segs + 2 * nseg, (int)nseg, items, norm_slots.data_ptr<float>(), (float)gscale, (float)max_norm, (float)lr,
-      (float)beta1, (float)beta2, (float)eps, (float)wd, bc1, bc2s, norm_out.data_ptr<float>());
+      (float)beta1, (float)beta2, (float)eps, (float)wd, bc1, bc2s, norm_out.data_ptr<float>(),
+      (hyper.has_value() && hyper->defined()) ? hyper->data_ptr<float>() : nullptr);
   check_launch("comm_adamw_shard");
 }
 

@@ -111,9 +111,10 @@ class FusedDPAdamW(FusedAdamW):
         self.err = torch.zeros(1, dtype=torch.int32, device=device)
         self.norm_out = torch.zeros(1, dtype=torch.float32, device=device)
         self.last_grad_norm = self.norm_out
-        self.epoch = 0
+        self.epoch = torch.zeros(1, dtype=torch.int32, device=device)  # advanced by the first barrier
         self.step_count = 0
         self._tab_key = None
+        self.graph_safe = True
 
     def grad_scale(self) -> float:
         return 1.0 / self.world
@@ -127,23 +128,28 @@ class FusedDPAdamW(FusedAdamW):
         return self._tab
 
     @torch.no_grad()
-    def step(self, closure=None):
+    def step(self, closure=None, hyper: torch.Tensor | None = None, schedule: tuple | None = None):
+        """One fused step; ``hyper``/``schedule`` as in :meth:`FusedAdamW.step`
+        (device-side step count and learning rate for CUDA-graph replay)."""
         loss = closure() if closure is not None else None
         E = ext()
         g = self.param_groups[0]
         self.step_count += 1
-        self.epoch += 1
         tab, nseg, items = self._shard_table()
         w, me = self.world, self.rank
-        E.comm_barrier(self.sig.ptrs, 0, self.epoch, w, me, self.err)     # all gradients complete
+        lr, b1, b2 = g["lr"], g["betas"][0], g["betas"][1]
+        if hyper is not None:
+            warm, total, mr = schedule if schedule is not None else (0, 1, 1.0)
+            E.adamw_hyper_step(hyper, g.get("initial_lr", lr), b1, b2, warm, total, mr, schedule is not None)
+        E.comm_barrier(self.sig.ptrs, 0, self.epoch, True, w, me, self.err)   # all gradients complete
         E.comm_reduce_shard(self._grad_buf.ptrs, self.lo, self.n, self.gsum, self.grad_scale(),
                             self.slots.ptrs, w, me)
-        E.comm_barrier(self.sig.ptrs, 1, self.epoch, w, me, self.err)     # all shard norms published
+        E.comm_barrier(self.sig.ptrs, 1, self.epoch, False, w, me, self.err)  # all shard norms published
         E.comm_adamw_shard(self.gsum, self.master, self.exp_avg, self.exp_avg_sq, self._param_buf.ptrs,
                            self.lo, w, tab, nseg, items, self.slots.local.view(torch.float32),
-                           self.grad_scale(), self.max_grad_norm, g["lr"], g["betas"][0], g["betas"][1],
-                           g["eps"], g["weight_decay"], self.step_count, self.norm_out)
-        E.comm_barrier(self.sig.ptrs, 2, self.epoch, w, me, self.err)     # every rank's weights written
+                           self.grad_scale(), self.max_grad_norm, lr, b1, b2, g["eps"], g["weight_decay"],
+                           self.step_count, self.norm_out, hyper)
+        E.comm_barrier(self.sig.ptrs, 2, self.epoch, False, w, me, self.err)  # every rank's weights written
         return loss
 
     def check_errors(self) -> None:

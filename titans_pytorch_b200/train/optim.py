@@ -146,6 +146,7 @@ class FusedAdamW(torch.optim.Optimizer):
         self._tab_key = None
         self._tab = None
         self.last_grad_norm: torch.Tensor | None = None
+        self.graph_safe = self.kernels  # the step can be captured in a CUDA graph
 
     # torch.optim API -----------------------------------------------------
     def zero_grad(self, set_to_none: bool = True) -> None:  # noqa: ARG002 (flat grads are reused)

@@ -80,10 +80,11 @@ class Trainer:
         self._graph = None
         self._eager_graph_steps = 0
         if self.cfg.cuda_graph:
-            if self.device.type != "cuda" or engine is not None or self.cfg.gradient_accumulation_steps != 1:
-                raise ValueError("cuda_graph needs one CUDA device, no data-parallel engine and no accumulation")
-            if not getattr(self.optimizer, "kernels", False):
-                raise ValueError("cuda_graph needs the fused optimizer kernels")
+            if self.device.type != "cuda" or self.cfg.gradient_accumulation_steps != 1:
+                raise ValueError("cuda_graph needs a CUDA device and no gradient accumulation")
+            if not getattr(self.optimizer, "graph_safe", False):
+                raise ValueError("cuda_graph needs a graph-safe optimizer (fused kernels; the fused "
+                                 "data-parallel engine, not the collective one)")
 
     def _to_device(self, t: torch.Tensor) -> torch.Tensor:
         return t.to(self.device, non_blocking=True)
@@ -159,6 +160,8 @@ class Trainer:
         with torch.cuda.graph(g):
             loss = self.loss_fn(self._static_ids, self._static_labels)
             loss.backward()
+            if self.engine is not None:
+                self.engine.reduce_gradients(opt)
             opt.step(hyper=self._hyper, schedule=sched)
             opt.zero_grad()
             self._static_loss = loss.detach()

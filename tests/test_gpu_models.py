@@ -108,3 +108,25 @@ def test_cuda_graph_training_matches_eager(kind):
         assert abs(la - lb) <= 2e-3 * abs(la), (step, la, lb)
     for pa, pb in zip(ta.model.parameters(), tb_.model.parameters()):
         torch.testing.assert_close(pa.float(), pb.float(), atol=2e-2, rtol=2e-2)
+
+
+@pytest.mark.parametrize("kind", ["mac", "mag"])
+def test_graphed_forward_chains_states_like_eager_calls(kind):
+    from titans_pytorch_b200.inference.generate import GraphedForward
+
+    cfg = T.TitansConfig(dim=128, num_heads=2, num_layers=2, vocab_size=512, chunk_size=64, window_size=32,
+                         num_persistent_tokens=4, dropout=0.0, max_seq_len=1024)
+    torch.manual_seed(0)
+    m = T.create_model(kind, cfg).to("cuda", torch.bfloat16).eval()
+    ids = torch.randint(0, 512, (2, 64 * 5), device="cuda")
+    with torch.no_grad():
+        _, st = m(ids[:, :64])
+        runner = GraphedForward(m, 2, 64, st)
+        eager_st = st
+        for i in range(1, 5):
+            want, eager_st = m(ids[:, 64 * i:64 * (i + 1)], states=eager_st)
+            got, got_st = runner(ids[:, 64 * i:64 * (i + 1)])
+            torch.testing.assert_close(got.float(), want.float(), atol=2e-2, rtol=2e-2)
+    for a, b in zip(got_st, eager_st):
+        for x, y in zip(a.weights, b.weights):
+            torch.testing.assert_close(x.float(), y.float(), atol=2e-2, rtol=2e-2)

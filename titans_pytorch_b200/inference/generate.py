@@ -111,6 +111,47 @@ def prefill(model, input_ids: torch.Tensor, states=None, chunk: int | None = Non
     return last, states
 
 
+class GraphedForward:
+    """``model(x, states)`` for one fixed input shape, captured in a CUDA graph.
+
+    The memory states are chained in place: each replay reads the states the
+    previous replay left in ``self.states`` and overwrites them with the new
+    ones, so prefilling a long prompt or decoding token by token is a series of
+    replays with only an input copy in between.  ``states`` (from an eager call
+    of the same model) seeds the chain; it is copied, not kept.
+    """
+
+    def __init__(self, model, batch: int, length: int, states, warmup: int = 2) -> None:
+        dev = next(model.parameters()).device
+        self.x = torch.zeros(batch, length, dtype=torch.long, device=dev)
+        self.states = [s.clone() for s in states]
+        cur = torch.cuda.current_stream(dev)
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(cur)
+        with torch.no_grad(), torch.cuda.stream(side):
+            for _ in range(warmup):
+                model(self.x, states=[s.clone() for s in self.states])
+        cur.wait_stream(side)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.no_grad(), torch.cuda.graph(self.graph):
+            logits, new = model(self.x, states=self.states)
+            for old, nxt in zip(self.states, new):
+                for a, b in zip(old.weights + old.momentum, nxt.weights + nxt.momentum):
+                    a.copy_(b)
+        self.logits = logits
+
+    def load_states(self, states) -> None:
+        for old, nxt in zip(self.states, states):
+            for a, b in zip(old.weights + old.momentum, nxt.weights + nxt.momentum):
+                a.copy_(b)
+
+    def __call__(self, x: torch.Tensor):
+        """Returns ``(logits, states)``; both are overwritten by the next call."""
+        self.x.copy_(x, non_blocking=True)
+        self.graph.replay()
+        return self.logits, self.states
+
+
 class OptimizedGenerator:
     """Generation front-end (`src/titans/optimized_inference.py:143-345`)."""
 

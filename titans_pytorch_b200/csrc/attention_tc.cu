@@ -210,6 +210,16 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         break;
       }
       tc::tc_fence_after();
+      // PV(it-1) of this tile was issued before S(it), and the tensor pipe
+      // completes in order, so it is done by now: O is stable, the P buffer free
+      if (it > 0) {
+        ok = tc::mbar_wait(bar_o_done + q, (it - 1) & 1, abort_flag, err);
+        if (!__all_sync(0xffffffffu, ok)) {
+          ok = false;
+          break;
+        }
+        tc::tc_fence_after();
+      }
       float s[BN];
 #pragma unroll
       for (int c = 0; c < BN / 32; ++c) {
@@ -242,38 +252,37 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       // raw-score max; the softmax scale (> 0) is folded into one FFMA before ex2
       const float mraw = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
                                fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
-      const float m_new = fmaxf(m_run, mraw * scale_log2);
+      const float m_cand = fmaxf(m_run, mraw * scale_log2);
+      // lazy rescale: the running max moves only when the tile's max exceeds it by
+      // more than 8 (log2 units), so P <= 2^8 and O is rescaled rarely
+      const bool grow = m_cand > m_run + 8.f;
+      const float m_new = grow ? m_cand : m_run;
       const float m_use = m_new == -INFINITY ? 0.f : m_new;
-      const float corr = ex2(m_run - m_use);
+      const float corr = grow ? ex2(m_run - m_use) : 1.f;
       float sm[8];
 #pragma unroll
       for (int k = 0; k < 8; ++k) sm[k] = 0.f;
-      uint32_t pk[BN / 2];
+      // P in 32-column pieces, each stored to shared memory (UMMA K-major) at once
 #pragma unroll
-      for (int c = 0; c < BN; c += 2) {
-        const float p0 = ex2(fmaf(s[c], scale_log2, -m_use)), p1 = ex2(fmaf(s[c + 1], scale_log2, -m_use));
-        sm[(c >> 1) & 7] += p0 + p1;
-        pk[c / 2] = pack2(p0, p1);
+      for (int c = 0; c < BN; c += 32) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int x = 0; x < 32; x += 2) {
+          const float p0 = ex2(fmaf(s[c + x], scale_log2, -m_use));
+          const float p1 = ex2(fmaf(s[c + x + 1], scale_log2, -m_use));
+          sm[(x >> 1) & 7] += p0 + p1;
+          pk[x >> 1] = pack2(p0, p1);
+        }
+        uint8_t* blk = sP + (c >> 6) * (BM * 128) + row * 128;
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) {
+          const int ch = ((c >> 5) & 1) * 4 + q4;
+          *reinterpret_cast<uint4*>(blk + ((ch ^ (row & 7)) << 4)) =
+              make_uint4(pk[4 * q4], pk[4 * q4 + 1], pk[4 * q4 + 2], pk[4 * q4 + 3]);
+        }
       }
       const float rs = ((sm[0] + sm[1]) + (sm[2] + sm[3])) + ((sm[4] + sm[5]) + (sm[6] + sm[7]));
       l_run = l_run * corr + rs;
-      // PV(it-1) of this tile done: O is stable and the P buffer is free
-      if (it > 0) {
-        ok = tc::mbar_wait(bar_o_done + q, (it - 1) & 1, abort_flag, err);
-        if (!__all_sync(0xffffffffu, ok)) {
-          ok = false;
-          break;
-        }
-        tc::tc_fence_after();
-      }
-#pragma unroll
-      for (int cb = 0; cb < 2; ++cb)
-#pragma unroll
-        for (int ch = 0; ch < 8; ++ch) {
-          const int x = cb * 32 + ch * 4;
-          *reinterpret_cast<uint4*>(sP + cb * (BM * 128) + row * 128 + ((ch ^ (row & 7)) << 4)) =
-              make_uint4(pk[x], pk[x + 1], pk[x + 2], pk[x + 3]);
-        }
       if (__any_sync(0xffffffffu, it > 0 && corr < 1.f)) {
 #pragma unroll
         for (int h = 0; h < HD / 32; ++h) {

@@ -175,3 +175,56 @@ def test_cli_pretrain_infer_eval_pretokenize(tmp_path, capsys):
     pretokenize.main(["--input", str(text), "--output", str(tmp_path / "tok"), "--seq-len", "32",
                       "--vocab-size", "128"])
     pretrain.main(common + ["--local-dataset", str(tmp_path / "tok"), "--max-steps", "2"])
+
+
+@pytest.mark.parametrize("kind", ["mac", "mag"])
+def test_weight_cache_does_not_outlive_a_forward(kind):
+    """Derived weights cached within one forward must reflect in-place weight updates."""
+    m = tiny(kind).eval()
+    ids = torch.randint(0, 64, (1, 40))
+    with torch.no_grad():
+        a, _ = m(ids)
+        for p in m.parameters():
+            p.mul_(1.5)
+        b, _ = m(ids)
+    fresh = tiny(kind).eval()
+    fresh.load_state_dict(m.state_dict())
+    with torch.no_grad():
+        c, _ = fresh(ids)
+    assert not torch.allclose(a, b)
+    torch.testing.assert_close(b, c)
+
+
+@pytest.mark.parametrize("kind", ["mal", "mag", "lmm"])
+def test_gradient_checkpointing_runs_update_once_and_matches(kind):
+    """Checkpointed blocks (memory update outside the recomputed region) equal plain blocks."""
+    import copy
+
+    from titans_pytorch_b200.ops.loss import cross_entropy
+    from titans_pytorch_b200.utils.perf import enable_gradient_checkpointing
+
+    a = tiny(kind)
+    b = copy.deepcopy(a)
+    enable_gradient_checkpointing(b)
+    calls = {"n": 0}
+    for blk in b.blocks:
+        orig = blk.memory._update
+
+        def counted(*args, _orig=orig, **kw):
+            calls["n"] += 1
+            return _orig(*args, **kw)
+
+        blk.memory._update = counted
+    ids = torch.randint(0, 64, (2, 33))
+    la, sa = a(ids[:, :-1])
+    lb, sb = b(ids[:, :-1])
+    cross_entropy(la, ids[:, 1:]).backward()
+    cross_entropy(lb, ids[:, 1:]).backward()
+    assert calls["n"] == len(b.blocks)  # once per block, not again in the recompute
+    torch.testing.assert_close(la, lb)
+    for pa, pb in zip(a.parameters(), b.parameters()):
+        if pa.grad is not None:
+            torch.testing.assert_close(pa.grad, pb.grad)
+    for s1, s2 in zip(sa, sb):
+        for x, y in zip(s1.weights, s2.weights):
+            torch.testing.assert_close(x, y)

@@ -169,12 +169,15 @@ __global__ void seq_mean_finish_kernel(const float* __restrict__ part, int split
   xm[e] = to_f<T>(from_f<T>(s / (float)Tn));
 }
 
-// grid (nblk, 3 gates); warp per output feature.
+// grid (ceil(D / 8), 3 gates), 8 warps: one warp per output feature o; the
+// lanes stream W[o, :] in 16-byte pieces against the B sequence means (shared
+// memory), eight samples at a time.
 // sig_part[gate, blk] = sum over (b, o in blk) sigmoid(z)
 template <typename T>
 __global__ void gate_gemv_kernel(const float* __restrict__ xm_g, const T* __restrict__ W0, const T* __restrict__ W1,
                                  const T* __restrict__ W2, const T* __restrict__ b0, const T* __restrict__ b1,
                                  const T* __restrict__ b2, float* __restrict__ sig_part, int B, int D) {
+  constexpr int V = Vec16<T>::N;
   extern __shared__ float xm[];  // [B, D] sequence means
   const int gate = blockIdx.y;
   const T* W = gate == 0 ? W0 : (gate == 1 ? W1 : W2);
@@ -182,16 +185,36 @@ __global__ void gate_gemv_kernel(const float* __restrict__ xm_g, const T* __rest
   for (int e = threadIdx.x; e < B * D; e += blockDim.x) xm[e] = xm_g[e];
   __syncthreads();
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  const int o = blockIdx.x * nw + wid;
   float local = 0.f;
-  for (int o = blockIdx.x * nw + wid; o < D; o += gridDim.x * nw) {
+  if (o < D) {
     const T* wr = W + (int64_t)o * D;
     const float bias = bb ? to_f<T>(bb[o]) : 0.f;
-    for (int b = 0; b < B; ++b) {
-      float acc = 0.f;
-      for (int d = lane; d < D; d += 32) acc += xm[b * D + d] * to_f<T>(wr[d]);
-      acc = warp_sum(acc) + bias;
-      // round the logit to the input dtype, as the reference's Linear output is
-      if (lane == 0) local += sigmoidf_(to_f<T>(from_f<T>(acc)));
+    for (int bs = 0; bs < B; bs += 8) {
+      const int nb = min(8, B - bs);
+      float acc[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+      for (int d = lane * V; d < D; d += 32 * V) {
+        float w[V];
+        load16<T>(wr + d, w);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          if (j < nb) {
+            const float* xr = xm + (bs + j) * D + d;
+#pragma unroll
+            for (int v = 0; v < V; ++v) acc[j] += w[v] * xr[v];
+          }
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        if (j < nb) {
+          const float z = warp_sum(acc[j]) + bias;
+          // round the logit to the input dtype, as the reference's Linear output is
+          if (lane == 0) local += sigmoidf_(to_f<T>(from_f<T>(z)));
+        }
+      }
     }
   }
   __shared__ float red[32];
@@ -224,7 +247,7 @@ at::Tensor memory_gates(const at::Tensor& x, const std::vector<at::Tensor>& ws, 
   const int splits = std::max(1, std::min(64, Tn / 64));
   at::Tensor part = at::empty({splits, B, D}, x.options().dtype(at::kFloat));
   at::Tensor gates = at::empty({3}, x.options().dtype(at::kFloat));
-  const int nblk = std::max(1, std::min(32, (D + 7) / 8));
+  const int nblk = (D + 7) / 8;  // 8 warps per block, one output feature per warp
   at::Tensor sig = at::empty({3, nblk}, x.options().dtype(at::kFloat));
   TB_DISPATCH_FLOAT(x.scalar_type(), "memory_gates", [&] {
     using T = scalar_t;
@@ -240,6 +263,7 @@ at::Tensor memory_gates(const at::Tensor& x, const std::vector<at::Tensor>& ws, 
     TORCH_CHECK(smem <= 200 * 1024, "memory_gates: B*D too large for one block's shared memory");
     if (smem > 48 * 1024)
       cudaFuncSetAttribute(gate_gemv_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    TORCH_CHECK(D % Vec16<T>::N == 0, "memory_gates: dim must be a multiple of ", Vec16<T>::N);
     at::Tensor xm = at::empty({B, D}, x.options().dtype(at::kFloat));
     seq_mean_finish_kernel<T><<<(B * D + 255) / 256, 256, 0, stream()>>>(part.data_ptr<float>(), splits,
                                                                         xm.data_ptr<float>(), B * D, Tn);

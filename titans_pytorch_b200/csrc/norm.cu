@@ -131,7 +131,8 @@ std::vector<at::Tensor> rms_norm_bwd(const at::Tensor& dy, const at::Tensor& x, 
   });
   check_launch("rms_norm_bwd");
   if (need_dw) {
-    colsum_kernel<<<(D + 255) / 256, 256, 0, stream()>>>(part.data_ptr<float>(), dw.data_ptr<float>(), blocks, D);
+    colsum_par_kernel<<<(D + 31) / 32, dim3(32, 16), 0, stream()>>>(part.data_ptr<float>(), dw.data_ptr<float>(),
+                                                                  blocks, D);
     check_launch("rms_norm_bwd colsum");
   }
   return {dx, dw};

@@ -90,4 +90,23 @@ static __global__ void colsum_kernel(const float* __restrict__ part, float* __re
   out[col] = s;
 }
 
+// The same column sums with more parallelism: block = 32 columns x 16 row
+// groups; each thread sums every 16th partial row of its column, then the 16
+// group sums are added in a fixed order (deterministic).
+static __global__ void colsum_par_kernel(const float* __restrict__ part, float* __restrict__ out, int G, int D) {
+  __shared__ float red[16][33];
+  const int col = blockIdx.x * 32 + threadIdx.x;
+  float s = 0.f;
+  if (col < D)
+    for (int g = threadIdx.y; g < G; g += 16) s += part[(int64_t)g * D + col];
+  red[threadIdx.y][threadIdx.x] = s;
+  __syncthreads();
+  if (threadIdx.y == 0 && col < D) {
+    float t = 0.f;
+#pragma unroll
+    for (int k = 0; k < 16; ++k) t += red[k][threadIdx.x];
+    out[col] = t;
+  }
+}
+
 }  // namespace tb

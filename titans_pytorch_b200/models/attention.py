@@ -78,8 +78,23 @@ class _AttentionBase(nn.Module):
         for m in (self.proj_q, self.proj_k, self.proj_v, self.proj_out):
             nn.init.normal_(m.weight, std=config.init_std)
 
+    # Set by the owning model: a per-forward cache of derived weights, so a MAC
+    # forward without autograd (inference) concatenates q|k|v once instead of
+    # once per segment.  With autograd the concatenation is rebuilt per use:
+    # sharing it would sum the segments' gradients out of place at the shared
+    # node instead of accumulating them in place into each weight's .grad.
+    _wcache: dict | None = None
+
     def _qkv_weight(self) -> torch.Tensor:
-        return torch.cat([self.proj_q.weight, self.proj_k.weight, self.proj_v.weight], dim=0)
+        key = (id(self), "qkv")
+        use = self._wcache is not None and self._wcache.get("active") and not torch.is_grad_enabled()
+        cache = self._wcache if use else None
+        if cache is not None and key in cache:
+            return cache[key]
+        w = torch.cat([self.proj_q.weight, self.proj_k.weight, self.proj_v.weight], dim=0)
+        if cache is not None:
+            cache[key] = w
+        return w
 
     def _attend(self, qkv, pkv, window):
         """qkv: [B, T, 3D]; pkv: [B or 1, P, 2D] or None -> [B, T, D] after proj_out."""

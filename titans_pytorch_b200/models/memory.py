@@ -166,10 +166,23 @@ class NeuralLongTermMemory(nn.Module):
         wq, bq = self._conv("conv_q")
         return conv_silu_norm(F.linear(x, self.proj_q.weight), wq, bq, True, self.use_kernels)
 
+    # per-forward cache of derived weights, set by the owning model (see SegmentedAttention)
+    _wcache: dict | None = None
+
+    def _kv_weight(self) -> torch.Tensor:
+        key = (id(self), "kv", torch.is_grad_enabled())
+        cache = self._wcache if self._wcache is not None and self._wcache.get("active") else None
+        if cache is not None and key in cache:
+            return cache[key]
+        w = torch.cat([self.proj_k.weight, self.proj_v.weight], dim=0)
+        if cache is not None:
+            cache[key] = w
+        return w
+
     @torch.no_grad()
     def _keys_values(self, x: torch.Tensor):
         D = self.dim
-        kv = F.linear(x, torch.cat([self.proj_k.weight, self.proj_v.weight], dim=0))
+        kv = F.linear(x, self._kv_weight())
         wk, bk = self._conv("conv_k")
         wv, bv = self._conv("conv_v")
         k = conv_silu_norm(kv[..., :D], wk, bk, True, self.use_kernels)
@@ -234,7 +247,7 @@ class NeuralLongTermMemory(nn.Module):
         q = conv_silu_norm(F.linear(x, self.proj_q.weight), wq, bq, False, self.use_kernels)
         q = F.normalize(self._split_heads(q), dim=-1)
         with torch.no_grad():
-            kv = F.linear(x, torch.cat([self.proj_k.weight, self.proj_v.weight], dim=0))
+            kv = F.linear(x, self._kv_weight())
             wk, bk = self._conv("conv_k")
             wv, bv = self._conv("conv_v")
             k = F.normalize(self._split_heads(conv_silu_norm(kv[..., :D], wk, bk, False, self.use_kernels)), dim=-1)
@@ -302,10 +315,13 @@ class NeuralLongTermMemory(nn.Module):
         return MemoryState(new_w, new_m).detach()
 
     def forward(self, x: torch.Tensor, state: MemoryState | None = None,
-                return_state: bool = True):
+                return_state: bool = True, update: bool = True):
         """Retrieve with the incoming memory and update it with ``x``.
 
-        Returns ``(proj_out(M_{t-1}(q)), new_state or None)``.
+        Returns ``(proj_out(M_{t-1}(q)), new_state or None)``.  ``update=False``
+        skips the (gradient-free) update and returns no state; activation
+        checkpointing uses it to run the update once, outside the recomputed
+        region.
         """
         if state is None:
             state = self.init_state(x.shape[0], x.device)
@@ -316,7 +332,7 @@ class NeuralLongTermMemory(nn.Module):
             out = F.linear(y, self.proj_out.weight)
             return (out, new_state) if return_state else (out, None)
         retrieved = self.memory(self._queries(x))
-        new_state = self._update(x, state)
+        new_state = self._update(x, state) if update else None
         out = F.linear(retrieved, self.proj_out.weight)
         return (out, new_state) if return_state else (out, None)
 

@@ -73,10 +73,14 @@ class MAGBlock(nn.Module):
         self.norm2 = _norm(config)
         self.dropout = nn.Dropout(config.dropout)
 
-    def forward(self, x: torch.Tensor, state: MemoryState | None = None):
+    def memory_input(self, x: torch.Tensor) -> torch.Tensor:
+        """The tensor the memory reads (and is updated with) for block input ``x``."""
+        return self.norm1(x)
+
+    def forward(self, x: torch.Tensor, state: MemoryState | None = None, update_memory: bool = True):
         n = self.norm1(x)
         y = x + self.dropout(self.attention(n, prefix=self.persistent(x.shape[0])))
-        m, new_state = self.memory(n, state=state)
+        m, new_state = self.memory(n, state=state, update=update_memory)
         out = y * m
         out = out + self.dropout(self.ffn(self.norm2(out)))
         return out, new_state
@@ -95,8 +99,11 @@ class MALBlock(nn.Module):
         self.norm3 = _norm(config)
         self.dropout = nn.Dropout(config.dropout)
 
-    def forward(self, x: torch.Tensor, state: MemoryState | None = None):
-        m, new_state = self.memory(self.norm1(x), state=state)
+    def memory_input(self, x: torch.Tensor) -> torch.Tensor:
+        return self.norm1(x)
+
+    def forward(self, x: torch.Tensor, state: MemoryState | None = None, update_memory: bool = True):
+        m, new_state = self.memory(self.norm1(x), state=state, update=update_memory)
         x = x + self.dropout(m)
         x = x + self.dropout(self.attention(self.norm2(x), prefix=self.persistent(x.shape[0])))
         x = x + self.dropout(self.ffn(self.norm3(x)))
@@ -113,8 +120,11 @@ class LMMBlock(nn.Module):
         self.norm2 = _norm(config)
         self.dropout = nn.Dropout(config.dropout)
 
-    def forward(self, x: torch.Tensor, state: MemoryState | None = None):
-        m, new_state = self.memory(self.norm1(x), state=state)
+    def memory_input(self, x: torch.Tensor) -> torch.Tensor:
+        return self.norm1(x)
+
+    def forward(self, x: torch.Tensor, state: MemoryState | None = None, update_memory: bool = True):
+        m, new_state = self.memory(self.norm1(x), state=state, update=update_memory)
         x = x + self.dropout(m)
         x = x + self.dropout(self.ffn(self.norm2(x)))
         return x, new_state
@@ -135,6 +145,11 @@ class _TitansLM(nn.Module):
         self.head = nn.Linear(config.dim, config.vocab_size, bias=False)
         self.head.weight = self.embed.weight
         nn.init.normal_(self.embed.weight, std=config.init_std)
+        # derived weights (concatenations) shared by the segments of one forward
+        self._wcache: dict = {}
+        for mod in self.modules():
+            if hasattr(type(mod), "_wcache") and mod is not self:
+                mod._wcache = self._wcache
 
     def _run_blocks(self, x, states):
         new_states = []
@@ -147,7 +162,12 @@ class _TitansLM(nn.Module):
         """Final-norm hidden states [B, T, D] and new memory states (no head GEMM)."""
         if states is None:
             states = [None] * len(self.blocks)
-        x, new_states = self._run_blocks(self.embed(input_ids), states)
+        self._wcache.clear()
+        self._wcache["active"] = True  # only while this forward runs
+        try:
+            x, new_states = self._run_blocks(self.embed(input_ids), states)
+        finally:
+            self._wcache.clear()  # weights change between forwards
         return self.norm(x), new_states
 
     def forward(self, input_ids: torch.Tensor, states: list[MemoryState] | None = None):
@@ -165,9 +185,14 @@ class TitansMAC(_TitansLM):
         x = self.embed(input_ids)
         cs = self.config.chunk_size
         outs = []
-        for s in range(0, x.shape[1], cs):
-            chunk, states = self._run_blocks(x[:, s:s + cs], states)
-            outs.append(chunk)
+        self._wcache.clear()
+        self._wcache["active"] = True  # only while this forward runs
+        try:
+            for s in range(0, x.shape[1], cs):
+                chunk, states = self._run_blocks(x[:, s:s + cs], states)
+                outs.append(chunk)
+        finally:
+            self._wcache.clear()  # weights change between forwards
         return self.norm(torch.cat(outs, dim=1)), states
 
 

@@ -110,8 +110,12 @@ def empty_cache_if_needed(threshold: float = 0.9) -> None:
 def enable_gradient_checkpointing(model: torch.nn.Module) -> torch.nn.Module:
     """Recompute each block's forward in the backward (non-reentrant checkpoint).
 
-    The memory update inside a block runs without autograd and is a pure
-    function of the block input, so recomputation reproduces it exactly.
+    The memory update has no gradient (its output, the next state, is
+    detached), so for blocks whose memory reads the block input (MAG, MAL,
+    LMM; reference semantics) it runs once, under ``no_grad`` before the
+    checkpointed region, and the region (recomputed in the backward) skips it.
+    Other blocks recompute their whole forward; the update is a pure function
+    of the block input, so the recomputation reproduces it exactly.
     """
     from torch.utils.checkpoint import checkpoint
 
@@ -119,9 +123,20 @@ def enable_gradient_checkpointing(model: torch.nn.Module) -> torch.nn.Module:
         if getattr(block, "_titans_ckpt", False):
             continue
         fwd = block.forward
+        split = hasattr(block, "memory_input") and getattr(block.memory, "paper", False) is False
 
-        def wrapped(x, state=None, _fwd=fwd):
-            return checkpoint(_fwd, x, state, use_reentrant=False)
+        if split:
+            def wrapped(x, state=None, _fwd=fwd, _blk=block):
+                mem = _blk.memory
+                if state is None:
+                    state = mem.init_state(x.shape[0], x.device)
+                with torch.no_grad():
+                    new_state = mem._update(_blk.memory_input(x), state)
+                out = checkpoint(lambda xx, st: _fwd(xx, st, update_memory=False)[0], x, state, use_reentrant=False)
+                return out, new_state
+        else:
+            def wrapped(x, state=None, _fwd=fwd):
+                return checkpoint(_fwd, x, state, use_reentrant=False)
 
         block.forward = wrapped
         block._titans_ckpt = True

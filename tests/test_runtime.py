@@ -228,3 +228,29 @@ def test_gradient_checkpointing_runs_update_once_and_matches(kind):
     for s1, s2 in zip(sa, sb):
         for x, y in zip(s1.weights, s2.weights):
             torch.testing.assert_close(x, y)
+
+
+@pytest.mark.parametrize("kind", ["mac", "mag"])
+def test_in_place_weight_grad_accumulation_matches_autograd(kind):
+    """Trainer backward (weight gradients added in place into the flat buffer) equals plain autograd."""
+    import copy
+
+    from titans_pytorch_b200.ops.linear import accumulate_weight_grads
+    from titans_pytorch_b200.ops.loss import cross_entropy
+    from titans_pytorch_b200.train.optim import FlatParamSpace
+
+    a = tiny(kind)
+    b = copy.deepcopy(a)
+    ids = torch.randint(0, 64, (2, 41))
+    loss_a = cross_entropy(a(ids[:, :-1])[0], ids[:, 1:])
+    loss_a.backward()
+    space = FlatParamSpace(b.parameters())
+    space.zero_grad()
+    with accumulate_weight_grads():
+        cross_entropy(b(ids[:, :-1])[0], ids[:, 1:]).backward()
+    for (n, pa), pb in zip(a.named_parameters(), b.parameters()):
+        if pa.grad is None:
+            continue
+        torch.testing.assert_close(pb.grad, pa.grad, atol=1e-6, rtol=1e-5, msg=n)
+    got = dict(zip([id(p) for p in space.params], space.got))
+    assert all(got[id(p)] for p in b.parameters() if p.grad is not None and p.grad.abs().sum() > 0)

@@ -16,6 +16,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from ..config import TitansConfig
+from ..ops.linear import linear
 from ..ops.attention import prefix_window_mask, window_attention
 
 
@@ -102,7 +103,17 @@ class _AttentionBase(nn.Module):
             qkv, pkv, self.num_heads, window=window, scale=self.scale,
             inv_freq=None if self.rope is None else self.rope.inv_freq,
             dropout_p=self.dropout.p, training=self.training, use_kernels=self.use_kernels)
-        return F.linear(o.reshape(*qkv.shape[:-1], self.dim), self.proj_out.weight)
+        return linear(o.reshape(*qkv.shape[:-1], self.dim), self.proj_out.weight)
+
+    def _project(self, x: torch.Tensor, kv_only: bool = False) -> torch.Tensor:
+        """x @ [Wq; Wk; Wv]^T (or [Wk; Wv] with ``kv_only``); weight gradients
+        accumulate in place under the trainer (see ``ops.linear``)."""
+        if not torch.is_grad_enabled():
+            w = self._qkv_weight()
+            return F.linear(x, w[self.dim:] if kv_only else w)
+        ws = (self.proj_k.weight, self.proj_v.weight) if kv_only else (
+            self.proj_q.weight, self.proj_k.weight, self.proj_v.weight)
+        return linear(x, *ws)
 
 
 class SlidingWindowAttention(_AttentionBase):
@@ -121,13 +132,12 @@ class SlidingWindowAttention(_AttentionBase):
         change with it (the argument is kept for API compatibility).
         """
         del seq_offset
-        w = self._qkv_weight()
-        qkv = F.linear(x, w)
+        qkv = self._project(x)
         pkv = None
         if prefix is not None and prefix.shape[1] > 0:
             if prefix.stride(0) == 0:  # batch-broadcast persistent tokens: project once
                 prefix = prefix[:1]
-            pkv = F.linear(prefix, w[self.dim:])
+            pkv = self._project(prefix, kv_only=True)
         return self._attend(qkv, pkv, self.window_size)
 
     # Mask helpers (same contract as the reference's, used by tests and debugging)
@@ -149,21 +159,19 @@ class SegmentedAttention(_AttentionBase):
     def forward(self, x: torch.Tensor, persistent: torch.Tensor | None = None,
                 memory: torch.Tensor | None = None) -> torch.Tensor:
         B = x.shape[0]
-        D = self.dim
-        w = self._qkv_weight()
-        qkv = F.linear(x, w)
+        qkv = self._project(x)
         parts = [p for p in (persistent, memory) if p is not None and p.shape[1] > 0]
         pkv = None
         if len(parts) == 1:
             pre = parts[0][:1] if parts[0].stride(0) == 0 else parts[0]
-            pkv = F.linear(pre, w[D:])
+            pkv = self._project(pre, kv_only=True)
         elif len(parts) == 2:
             if persistent.stride(0) == 0:
                 # shared persistent rows: project once, then broadcast over the batch
-                pkv_p = F.linear(persistent[:1], w[D:]).expand(B, -1, -1)
+                pkv_p = self._project(persistent[:1], kv_only=True).expand(B, -1, -1)
             else:
-                pkv_p = F.linear(persistent, w[D:])
-            pkv = torch.cat([pkv_p, F.linear(memory, w[D:])], dim=1)
+                pkv_p = self._project(persistent, kv_only=True)
+            pkv = torch.cat([pkv_p, self._project(memory, kv_only=True)], dim=1)
         return self._attend(qkv, pkv, None)
 
     def _create_causal_mask(self, seq_len: int, device) -> torch.Tensor:

@@ -34,6 +34,7 @@ from ..config import TitansConfig
 from ..ops.conv import conv_silu_norm
 from ..ops.memory import (activation_fn, memory_grads_reference, memory_step,
                           mlp_forward_reference)
+from ..ops.linear import linear
 from ..ops.memory_paper import head_blocks, memory_scan, memory_scan_reference
 
 
@@ -83,7 +84,15 @@ class MemoryMLP(nn.Module):
         return [layer.weight for layer in self.layers]
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        return mlp_forward_reference(x, self.weight_list(), self.config.activation)
+        # same math as mlp_forward_reference; the weight gradients go through
+        # ops.linear (accumulated in place under the trainer)
+        f = activation_fn(self.config.activation)
+        h = x
+        for i, layer in enumerate(self.layers):
+            h = linear(h, layer.weight)
+            if i < self.num_layers - 1:
+                h = f(h)
+        return h
 
     def get_weights(self) -> list[torch.Tensor]:
         return [layer.weight.detach().clone() for layer in self.layers]
@@ -164,7 +173,7 @@ class NeuralLongTermMemory(nn.Module):
 
     def _queries(self, x: torch.Tensor) -> torch.Tensor:
         wq, bq = self._conv("conv_q")
-        return conv_silu_norm(F.linear(x, self.proj_q.weight), wq, bq, True, self.use_kernels)
+        return conv_silu_norm(linear(x, self.proj_q.weight), wq, bq, True, self.use_kernels)
 
     # per-forward cache of derived weights, set by the owning model (see SegmentedAttention)
     _wcache: dict | None = None
@@ -333,7 +342,7 @@ class NeuralLongTermMemory(nn.Module):
             return (out, new_state) if return_state else (out, None)
         retrieved = self.memory(self._queries(x))
         new_state = self._update(x, state) if update else None
-        out = F.linear(retrieved, self.proj_out.weight)
+        out = linear(retrieved, self.proj_out.weight)
         return (out, new_state) if return_state else (out, None)
 
     def retrieve(self, queries: torch.Tensor, state: MemoryState) -> torch.Tensor:
@@ -341,7 +350,7 @@ class NeuralLongTermMemory(nn.Module):
         if self.paper:
             return F.linear(self._paper_retrieve(queries, state), self.proj_out.weight)
         self.memory.set_weights(state.weights)
-        return F.linear(self.memory(self._queries(queries)), self.proj_out.weight)
+        return linear(self.memory(self._queries(queries)), self.proj_out.weight)
 
 
 __all__ = ["MemoryState", "MemoryMLP", "NeuralLongTermMemory", "get_activation", "activation_fn"]

@@ -23,6 +23,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from ..config import TitansConfig
+from ..ops.linear import linear
 from .attention import SegmentedAttention, SlidingWindowAttention
 from .layers import FeedForward, RMSNorm
 from .memory import MemoryState, NeuralLongTermMemory
@@ -172,7 +173,7 @@ class _TitansLM(nn.Module):
 
     def forward(self, input_ids: torch.Tensor, states: list[MemoryState] | None = None):
         h, new_states = self.hidden_states(input_ids, states)
-        return F.linear(h, self.head.weight), new_states
+        return linear(h, self.head.weight), new_states
 
 
 class TitansMAC(_TitansLM):

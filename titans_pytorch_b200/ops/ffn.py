@@ -4,8 +4,10 @@ Reference: `src/titans/models.py:27-70` (FeedForward; its CUDA branch calls a
 Triton silu*mul kernel without a backward, `triton_kernels.py:412-440`).
 
 CUDA path: the gate and up projections run as ONE GEMM against the stacked
-weight ``[Wg; Wu]`` and the SiLU-product is computed by ``csrc/ffn.cu``
-(fwd/bwd) -- or, with the tcgen05 GEMM, inside that GEMM's epilogue.
+weight ``[Wg; Wu]`` and the SiLU-product is computed by the ``swiglu_fwd`` /
+``swiglu_bwd`` kernels of ``csrc/elementwise.cu``.  Weight gradients go
+through :func:`~titans_pytorch_b200.ops.linear.linear` (accumulated in place
+under the trainer).
 """
 
 from __future__ import annotations
@@ -14,6 +16,7 @@ import torch
 import torch.nn.functional as F
 
 from ._ext import ext, want_kernels
+from .linear import linear
 
 
 class _SwiGLUFn(torch.autograd.Function):
@@ -35,10 +38,10 @@ def swiglu_ffn(x: torch.Tensor, w_gate: torch.Tensor, w_up: torch.Tensor, w_down
                dropout_p: float = 0.0, training: bool = False,
                use_kernels: bool | None = None) -> torch.Tensor:
     if want_kernels(x, use_kernels):
-        gu = F.linear(x, torch.cat([w_gate, w_up], dim=0))
+        gu = linear(x, w_gate, w_up)
         h = _SwiGLUFn.apply(gu.view(-1, gu.shape[-1])).view(*x.shape[:-1], w_gate.shape[0])
     else:
         h = F.silu(F.linear(x, w_gate)) * F.linear(x, w_up)
     if dropout_p > 0.0 and training:
         h = F.dropout(h, dropout_p, True)
-    return F.linear(h, w_down)
+    return linear(h, w_down)

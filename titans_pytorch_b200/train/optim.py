@@ -85,6 +85,8 @@ class FlatParamSpace:
         self.got = [False] * len(plist)
         self._hooks = [p.register_post_accumulate_grad_hook(self._make_hook(i))
                        for i, p in enumerate(plist)]
+        for i, p in enumerate(plist):  # for gradients written in place (ops.linear)
+            p._titans_grad_mark = self._make_hook(i)
 
     def _make_hook(self, i):
         def hook(_p):

@@ -16,6 +16,7 @@ from dataclasses import dataclass
 
 import torch
 
+from ..ops.linear import accumulate_weight_grads
 from ..ops.loss import cross_entropy
 from .optim import FusedAdamW
 
@@ -106,7 +107,8 @@ class Trainer:
         labels = self._to_device(batch["labels"])
         accum = self.cfg.gradient_accumulation_steps
         loss = self.loss_fn(ids, labels)
-        (loss / accum if accum > 1 else loss).backward()
+        with accumulate_weight_grads():
+            (loss / accum if accum > 1 else loss).backward()
         self._micro += 1
         if self._micro % accum == 0:
             self.optimizer_step()
@@ -133,7 +135,8 @@ class Trainer:
                 ids = self._to_device(batch["input_ids"])
                 labels = self._to_device(batch["labels"])
                 loss = self.loss_fn(ids, labels)
-                loss.backward()
+                with accumulate_weight_grads():
+                    loss.backward()
                 self.optimizer_step()
             cur.wait_stream(side)
             self._eager_graph_steps += 1
@@ -159,7 +162,8 @@ class Trainer:
         saved_count = opt.step_count
         with torch.cuda.graph(g):
             loss = self.loss_fn(self._static_ids, self._static_labels)
-            loss.backward()
+            with accumulate_weight_grads():
+                loss.backward()
             if self.engine is not None:
                 self.engine.reduce_gradients(opt)
             opt.step(hyper=self._hyper, schedule=sched)

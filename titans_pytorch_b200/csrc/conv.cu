@@ -33,9 +33,46 @@ __device__ __forceinline__ void load_cols_f32(const float* __restrict__ p, int c
   }
 }
 
+// Weights in the parameter's own layout and dtype: w[d][j] ([D, K], the
+// Conv1d weight [D, 1, K] viewed), so no transposed fp32 copy is made per
+// call.  The KS taps of V consecutive columns are KS*V contiguous elements,
+// read as 16-byte pieces (the column start is a multiple of V).
+template <typename T, int KS>
+__device__ __forceinline__ void load_taps(const T* __restrict__ w, int col, float (&o)[KS][Vec16<T>::N]) {
+  constexpr int V = Vec16<T>::N;
+  constexpr int NB = KS * V * (int)sizeof(T);
+  const T* src = w + (int64_t)col * KS;
+  if constexpr (NB % 16 == 0) {
+    uint4 buf[NB / 16];
+#pragma unroll
+    for (int i = 0; i < NB / 16; ++i) buf[i] = reinterpret_cast<const uint4*>(src)[i];
+    const T* e = reinterpret_cast<const T*>(buf);
+#pragma unroll
+    for (int i = 0; i < V; ++i)
+#pragma unroll
+      for (int j = 0; j < KS; ++j) o[j][i] = to_f<T>(e[i * KS + j]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < V; ++i)
+#pragma unroll
+      for (int j = 0; j < KS; ++j) o[j][i] = to_f<T>(src[i * KS + j]);
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ void load_bias(const T* __restrict__ b, int col, float (&o)[Vec16<T>::N]) {
+  constexpr int V = Vec16<T>::N;
+  if (b) {
+    load16<T>(b + col, o);
+  } else {
+#pragma unroll
+    for (int i = 0; i < V; ++i) o[i] = 0.f;
+  }
+}
+
 template <typename T, int KS>
 __global__ void __launch_bounds__(512) conv_fwd_rows(const T* __restrict__ x, int64_t sb, int64_t st,
-                                                     const float* __restrict__ wt, const float* __restrict__ bias,
+                                                     const T* __restrict__ wt, const T* __restrict__ bias,
                                                      T* __restrict__ y, int64_t rows, int Tn, int D, bool normalize) {
   constexpr int V = Vec16<T>::N;
   __shared__ float red[32][33];
@@ -58,15 +95,14 @@ __global__ void __launch_bounds__(512) conv_fwd_rows(const T* __restrict__ x, in
         for (int i = 0; i < V; ++i) xv[j][i] = 0.f;
     }
     float acc[V];
-    load_cols_f32(bias, col, acc);
+    load_bias<T>(bias, col, acc);
     if (wt) {
+      float wj[KS][V];
+      load_taps<T, KS>(wt, col, wj);
 #pragma unroll
-      for (int j = 0; j < KS; ++j) {
-        float wj[V];
-        load_cols_f32(wt + (int64_t)j * D, col, wj);
+      for (int j = 0; j < KS; ++j)
 #pragma unroll
-        for (int i = 0; i < V; ++i) acc[i] += wj[i] * xv[j][i];
-      }
+        for (int i = 0; i < V; ++i) acc[i] += wj[j][i] * xv[j][i];
     } else {
 #pragma unroll
       for (int i = 0; i < V; ++i) acc[i] += xv[KS - 1][i];
@@ -96,8 +132,8 @@ __global__ void __launch_bounds__(512) conv_fwd_rows(const T* __restrict__ x, in
 // dc = d(loss)/d(conv output) (fp32, [rows, D]); without a conv it writes dx directly.
 template <typename T, int KS>
 __global__ void __launch_bounds__(512) conv_bwd_a_rows(const T* __restrict__ dy, const T* __restrict__ x,
-                                                       int64_t sb, int64_t st, const float* __restrict__ wt,
-                                                       const float* __restrict__ bias, float* __restrict__ dc,
+                                                       int64_t sb, int64_t st, const T* __restrict__ wt,
+                                                       const T* __restrict__ bias, float* __restrict__ dc,
                                                        T* __restrict__ dx_direct, int64_t rows, int Tn, int D,
                                                        bool normalize) {
   constexpr int V = Vec16<T>::N;
@@ -121,15 +157,14 @@ __global__ void __launch_bounds__(512) conv_bwd_a_rows(const T* __restrict__ dy,
         for (int i = 0; i < V; ++i) xv[j][i] = 0.f;
     }
     load16<T>(dy + r * D + col, g);
-    load_cols_f32(bias, col, pre);
+    load_bias<T>(bias, col, pre);
     if (wt) {
+      float wj[KS][V];
+      load_taps<T, KS>(wt, col, wj);
 #pragma unroll
-      for (int j = 0; j < KS; ++j) {
-        float wj[V];
-        load_cols_f32(wt + (int64_t)j * D, col, wj);
+      for (int j = 0; j < KS; ++j)
 #pragma unroll
-        for (int i = 0; i < V; ++i) pre[i] += wj[i] * xv[j][i];
-      }
+        for (int i = 0; i < V; ++i) pre[i] += wj[j][i] * xv[j][i];
     } else {
 #pragma unroll
       for (int i = 0; i < V; ++i) pre[i] += xv[KS - 1][i];
@@ -171,7 +206,7 @@ __global__ void __launch_bounds__(512) conv_bwd_a_rows(const T* __restrict__ dy,
 // dw[j] += dc[t] x[t-KS+1+j]; db += dc[t].  part: [splits*B][KS+1][D]
 template <typename T, int KS, int U>
 __global__ void __launch_bounds__(256) conv_bwd_b_rows(const float* __restrict__ dc, const T* __restrict__ x,
-                                                       int64_t sb, int64_t st, const float* __restrict__ wt,
+                                                       int64_t sb, int64_t st, const T* __restrict__ wt,
                                                        T* __restrict__ dx, float* __restrict__ part, int Tn, int D,
                                                        int rows_per_split) {
   constexpr int V = Vec16<T>::N;
@@ -183,12 +218,11 @@ __global__ void __launch_bounds__(256) conv_bwd_b_rows(const float* __restrict__
   const T* xb = x + (int64_t)b * sb + col;
   const float* dcb = dc + (int64_t)b * Tn * D + col;
   float w[KS][V], aw[KS][V], ab[V];
+  load_taps<T, KS>(wt, col, w);
 #pragma unroll
-  for (int j = 0; j < KS; ++j) {
-    load_cols_f32(wt + (int64_t)j * D, col, w[j]);
+  for (int j = 0; j < KS; ++j)
 #pragma unroll
     for (int i = 0; i < V; ++i) aw[j][i] = 0.f;
-  }
 #pragma unroll
   for (int i = 0; i < V; ++i) ab[i] = 0.f;
   for (int t0 = ts; t0 < te; t0 += U) {
@@ -286,9 +320,19 @@ __global__ void colsum_kernel2(const float* __restrict__ part, float* __restrict
     TORCH_CHECK(false, NAME, ": bf16 or fp32 only, got ", dtype); \
   }()
 
-static at::Tensor conv_wt(const c10::optional<at::Tensor>& w, int D) {
+// [D, 1, K] Conv1d weight -> [D, K] in the activation dtype (a view when it
+// already is contiguous and of that dtype, as model parameters are)
+static at::Tensor conv_wt(const c10::optional<at::Tensor>& w, int D, at::ScalarType dt) {
   if (!w.has_value() || !w->defined()) return at::Tensor();
-  return w->reshape({D, -1}).t().contiguous().to(at::kFloat);  // [D,1,K] -> [K, D] fp32
+  at::Tensor t = w->reshape({D, -1}).to(dt).contiguous();
+  TORCH_CHECK(aligned16(t), "conv_silu_norm: weight must be 16-byte aligned");
+  return t;
+}
+static at::Tensor conv_bias(const c10::optional<at::Tensor>& b, at::ScalarType dt) {
+  if (!b.has_value() || !b->defined()) return at::Tensor();
+  at::Tensor t = b->to(dt).contiguous();
+  TORCH_CHECK(aligned16(t), "conv_silu_norm: bias must be 16-byte aligned");
+  return t;
 }
 
 static void check_x(const at::Tensor& x, int V) {
@@ -307,9 +351,9 @@ at::Tensor conv_silu_norm_fwd(const at::Tensor& x, const c10::optional<at::Tenso
   TB_CHECK_CUDA(x);
   const at::cuda::CUDAGuard g(x.device());
   const int B = x.size(0), Tn = x.size(1), D = x.size(2);
-  at::Tensor wt = conv_wt(w, D);
-  const int K = wt.defined() ? wt.size(0) : 1;
-  at::Tensor bias = (b.has_value() && b->defined()) ? b->to(at::kFloat).contiguous() : at::Tensor();
+  at::Tensor wt = conv_wt(w, D, x.scalar_type());
+  const int K = wt.defined() ? wt.size(1) : 1;
+  at::Tensor bias = conv_bias(b, x.scalar_type());
   at::Tensor y = at::empty({B, Tn, D}, x.options());
   const int64_t rows = (int64_t)B * Tn;
   if (rows == 0) return y;
@@ -319,8 +363,8 @@ at::Tensor conv_silu_norm_fwd(const at::Tensor& x, const c10::optional<at::Tenso
     const dim3 blk = row_block(threads_for(D, V));
     const int64_t grid = (rows + blk.y - 1) / blk.y;
     TB_KS_SWITCH(K, conv_fwd_rows<scalar_t, KS><<<grid, blk, 0, stream()>>>(
-        (const scalar_t*)x.data_ptr(), x.stride(0), x.stride(1), wt.defined() ? wt.data_ptr<float>() : nullptr,
-        bias.defined() ? bias.data_ptr<float>() : nullptr, (scalar_t*)y.data_ptr(), rows, Tn, D, normalize));
+        (const scalar_t*)x.data_ptr(), x.stride(0), x.stride(1), wt.defined() ? (const scalar_t*)wt.data_ptr() : nullptr,
+        bias.defined() ? (const scalar_t*)bias.data_ptr() : nullptr, (scalar_t*)y.data_ptr(), rows, Tn, D, normalize));
   });
   check_launch("conv_silu_norm_fwd");
   return y;
@@ -333,9 +377,9 @@ std::vector<at::Tensor> conv_silu_norm_bwd(const at::Tensor& dy, const at::Tenso
   const at::cuda::CUDAGuard g(x.device());
   const int B = x.size(0), Tn = x.size(1), D = x.size(2);
   at::Tensor dyc = contig16(dy.to(x.scalar_type()));
-  at::Tensor wt = conv_wt(w, D);
-  const int K = wt.defined() ? wt.size(0) : 1;
-  at::Tensor bias = (b.has_value() && b->defined()) ? b->to(at::kFloat).contiguous() : at::Tensor();
+  at::Tensor wt = conv_wt(w, D, x.scalar_type());
+  const int K = wt.defined() ? wt.size(1) : 1;
+  at::Tensor bias = conv_bias(b, x.scalar_type());
   at::Tensor dx = at::empty({B, Tn, D}, x.options());
   at::Tensor dw = at::empty({0}, x.options().dtype(at::kFloat)), db = at::empty({0}, x.options().dtype(at::kFloat));
   const int64_t rows = (int64_t)B * Tn;
@@ -349,7 +393,7 @@ std::vector<at::Tensor> conv_silu_norm_bwd(const at::Tensor& dy, const at::Tenso
     const int64_t grid = (rows + blk.y - 1) / blk.y;
     TB_KS_SWITCH(K, conv_bwd_a_rows<scalar_t, KS><<<grid, blk, 0, stream()>>>(
         (const scalar_t*)dyc.data_ptr(), (const scalar_t*)x.data_ptr(), x.stride(0), x.stride(1),
-        wt.defined() ? wt.data_ptr<float>() : nullptr, bias.defined() ? bias.data_ptr<float>() : nullptr,
+        wt.defined() ? (const scalar_t*)wt.data_ptr() : nullptr, bias.defined() ? (const scalar_t*)bias.data_ptr() : nullptr,
         dc.defined() ? dc.data_ptr<float>() : nullptr, (scalar_t*)dx.data_ptr(), rows, Tn, D, normalize));
     check_launch("conv_silu_norm_bwd_a");
     if (wt.defined()) {
@@ -362,7 +406,7 @@ std::vector<at::Tensor> conv_silu_norm_bwd(const at::Tensor& dy, const at::Tenso
       const int bx = std::min(tpr, 256);
       dim3 g2(splits, B, (tpr + bx - 1) / bx);
       TB_KS_SWITCH(K, conv_bwd_b_rows<scalar_t, KS, 2><<<g2, bx, 0, stream()>>>(
-          dc.data_ptr<float>(), (const scalar_t*)x.data_ptr(), x.stride(0), x.stride(1), wt.data_ptr<float>(),
+          dc.data_ptr<float>(), (const scalar_t*)x.data_ptr(), x.stride(0), x.stride(1), (const scalar_t*)wt.data_ptr(),
           (scalar_t*)dx.data_ptr(), need_wgrad ? part.data_ptr<float>() : nullptr, Tn, D, rps));
       check_launch("conv_silu_norm_bwd_b");
       if (need_wgrad) {

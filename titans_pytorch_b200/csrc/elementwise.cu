@@ -169,25 +169,24 @@ __global__ void seq_mean_finish_kernel(const float* __restrict__ part, int split
   xm[e] = to_f<T>(from_f<T>(s / (float)Tn));
 }
 
-// grid (ceil(D / 8), 3 gates), 8 warps: one warp per output feature o; the
-// lanes stream W[o, :] in 16-byte pieces against the B sequence means (shared
-// memory), eight samples at a time.
+// grid (ceil(D / 32), 3 gates), 8 warps of 4 output features each; the lanes
+// stream W[o, :] in 16-byte pieces against the B sequence means (read through
+// L1 as float4), eight samples at a time.
 // sig_part[gate, blk] = sum over (b, o in blk) sigmoid(z)
 template <typename T>
-__global__ void gate_gemv_kernel(const float* __restrict__ xm_g, const T* __restrict__ W0, const T* __restrict__ W1,
+__global__ void gate_gemv_kernel(const float* __restrict__ xm, const T* __restrict__ W0, const T* __restrict__ W1,
                                  const T* __restrict__ W2, const T* __restrict__ b0, const T* __restrict__ b1,
                                  const T* __restrict__ b2, float* __restrict__ sig_part, int B, int D) {
   constexpr int V = Vec16<T>::N;
-  extern __shared__ float xm[];  // [B, D] sequence means
+  constexpr int ROWS = 4;
   const int gate = blockIdx.y;
   const T* W = gate == 0 ? W0 : (gate == 1 ? W1 : W2);
   const T* bb = gate == 0 ? b0 : (gate == 1 ? b1 : b2);
-  for (int e = threadIdx.x; e < B * D; e += blockDim.x) xm[e] = xm_g[e];
-  __syncthreads();
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  const int o = blockIdx.x * nw + wid;
   float local = 0.f;
-  if (o < D) {
+  for (int r = 0; r < ROWS; ++r) {
+    const int o = (blockIdx.x * nw + wid) * ROWS + r;
+    if (o >= D) break;
     const T* wr = W + (int64_t)o * D;
     const float bias = bb ? to_f<T>(bb[o]) : 0.f;
     for (int bs = 0; bs < B; bs += 8) {
@@ -201,9 +200,12 @@ __global__ void gate_gemv_kernel(const float* __restrict__ xm_g, const T* __rest
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           if (j < nb) {
-            const float* xr = xm + (bs + j) * D + d;
+            const float4* xr = reinterpret_cast<const float4*>(xm + (int64_t)(bs + j) * D + d);
 #pragma unroll
-            for (int v = 0; v < V; ++v) acc[j] += w[v] * xr[v];
+            for (int v4 = 0; v4 < V / 4; ++v4) {
+              const float4 q = __ldg(xr + v4);
+              acc[j] += w[4 * v4] * q.x + w[4 * v4 + 1] * q.y + w[4 * v4 + 2] * q.z + w[4 * v4 + 3] * q.w;
+            }
           }
         }
       }
@@ -247,7 +249,7 @@ at::Tensor memory_gates(const at::Tensor& x, const std::vector<at::Tensor>& ws, 
   const int splits = std::max(1, std::min(64, Tn / 64));
   at::Tensor part = at::empty({splits, B, D}, x.options().dtype(at::kFloat));
   at::Tensor gates = at::empty({3}, x.options().dtype(at::kFloat));
-  const int nblk = (D + 7) / 8;  // 8 warps per block, one output feature per warp
+  const int nblk = (D + 31) / 32;  // 8 warps per block, 4 output features per warp
   at::Tensor sig = at::empty({3, nblk}, x.options().dtype(at::kFloat));
   TB_DISPATCH_FLOAT(x.scalar_type(), "memory_gates", [&] {
     using T = scalar_t;
@@ -259,16 +261,12 @@ at::Tensor memory_gates(const at::Tensor& x, const std::vector<at::Tensor>& ws, 
     dim3 g1((D + 127) / 128, B, splits);
     seq_sum_kernel<T><<<g1, 128, 0, stream()>>>((const T*)x.data_ptr(), x.stride(0), x.stride(1),
                                                  part.data_ptr<float>(), B, Tn, D, splits);
-    const size_t smem = (size_t)B * D * sizeof(float);
-    TORCH_CHECK(smem <= 200 * 1024, "memory_gates: B*D too large for one block's shared memory");
-    if (smem > 48 * 1024)
-      cudaFuncSetAttribute(gate_gemv_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     TORCH_CHECK(D % Vec16<T>::N == 0, "memory_gates: dim must be a multiple of ", Vec16<T>::N);
     at::Tensor xm = at::empty({B, D}, x.options().dtype(at::kFloat));
     seq_mean_finish_kernel<T><<<(B * D + 255) / 256, 256, 0, stream()>>>(part.data_ptr<float>(), splits,
                                                                         xm.data_ptr<float>(), B * D, Tn);
     dim3 g2(nblk, 3);
-    gate_gemv_kernel<T><<<g2, 256, smem, stream()>>>(
+    gate_gemv_kernel<T><<<g2, 256, 0, stream()>>>(
         xm.data_ptr<float>(), (const T*)wc[0].data_ptr(), (const T*)wc[1].data_ptr(),
         (const T*)wc[2].data_ptr(), bc[0].defined() ? (const T*)bc[0].data_ptr() : nullptr,
         bc[1].defined() ? (const T*)bc[1].data_ptr() : nullptr, bc[2].defined() ? (const T*)bc[2].data_ptr() : nullptr,

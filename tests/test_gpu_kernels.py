@@ -253,3 +253,27 @@ def test_attention_tcgen05_backward(case):
     assert E.kernel_error_status(0, True) == 0
     for x, y in zip(a, r):
         assert rel_err(x, y) < 1e-2
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("D", [768, 1536])
+def test_fused_add_rms_norm_kernel(dtype, D):
+    from titans_pytorch_b200.ops.norm import fused_add_rms_norm
+
+    torch.manual_seed(5)
+    x = torch.randn(3, 37, D, device=DEV, dtype=dtype, requires_grad=True)
+    r = torch.randn(3, 37, D, device=DEV, dtype=dtype, requires_grad=True)
+    w = (torch.rand(D, device=DEV) + 0.5).to(dtype).requires_grad_(True)
+    h, y = fused_add_rms_norm(x, r, w, 1e-6, use_kernels=True)
+    xf, rf, wf = (t.detach().float().requires_grad_(True) for t in (x, r, w))
+    hf = xf + rf
+    yf = hf * torch.rsqrt(hf.pow(2).mean(-1, keepdim=True) + 1e-6) * wf
+    tol = dict(atol=2e-2, rtol=2e-2) if dtype == torch.bfloat16 else dict(atol=1e-4, rtol=1e-4)
+    torch.testing.assert_close(h.float(), hf, **tol)
+    torch.testing.assert_close(y.float(), yf, **tol)
+    dh, dy = torch.randn_like(hf), torch.randn_like(yf)
+    (h.float() * dh + y.float() * dy).sum().backward()
+    (hf * dh + yf * dy).sum().backward()
+    torch.testing.assert_close(x.grad.float(), xf.grad, **tol)
+    torch.testing.assert_close(r.grad.float(), rf.grad, **tol)
+    torch.testing.assert_close(w.grad.float(), wf.grad, atol=0.5 if dtype == torch.bfloat16 else 1e-2, rtol=2e-2)

@@ -254,3 +254,42 @@ def test_in_place_weight_grad_accumulation_matches_autograd(kind):
         torch.testing.assert_close(pb.grad, pa.grad, atol=1e-6, rtol=1e-5, msg=n)
     got = dict(zip([id(p) for p in space.params], space.got))
     assert all(got[id(p)] for p in b.parameters() if p.grad is not None and p.grad.abs().sum() > 0)
+
+
+def test_p17_utilities():
+    from titans_pytorch_b200.utils import perf as P
+
+    torch.manual_seed(0)
+    g, u = torch.randn(3, 8), torch.randn(3, 8)
+    torch.testing.assert_close(P.fused_silu_mul(g, u), torch.nn.functional.silu(g) * u)
+    x, r, w = torch.randn(2, 5, 16), torch.randn(2, 5, 16), torch.rand(16) + 0.5
+    h, y = P.fused_add_rms_norm(x, r, w, 1e-6)
+    torch.testing.assert_close(h, x + r)
+    torch.testing.assert_close(y, (x + r) * torch.rsqrt((x + r).pow(2).mean(-1, keepdim=True) + 1e-6) * w)
+    wg, wu, wd = torch.randn(32, 16) * 0.1, torch.randn(32, 16) * 0.1, torch.randn(16, 32) * 0.1
+    torch.testing.assert_close(P.fused_linear_silu_linear(x, wg, wu, wd),
+                               torch.nn.functional.linear(torch.nn.functional.silu(x @ wg.t()) * (x @ wu.t()), wd))
+    with P.CUDAStreamManager(2).stream(1):
+        pass
+    m = tiny("mag").eval()
+    ids = torch.randint(0, 64, (2, 6))
+    logits, st = P.optimized_generate_step(m, ids)
+    assert logits.shape == (2, 64) and len(st) == 2
+
+
+def test_speculative_decode_equals_windowed_greedy():
+    from titans_pytorch_b200.utils.perf import speculative_decode
+
+    m = tiny("mag").eval()  # window 8 <= context 16
+    draft = tiny("mag").eval()
+    with torch.no_grad():
+        for p in draft.parameters():
+            p.add_(0.05 * torch.randn_like(p))  # a different (worse) draft
+    ids = torch.randint(0, 64, (2, 20))
+    got = speculative_decode(m, draft, ids, num_speculative_tokens=3, max_new_tokens=10, context=16)
+    want = ids
+    with torch.no_grad():
+        for _ in range(10):
+            lg, _ = m(want[:, -16:])
+            want = torch.cat([want, lg[:, -1:].argmax(-1)], 1)
+    assert torch.equal(got, want)

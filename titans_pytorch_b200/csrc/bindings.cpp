@@ -7,7 +7,8 @@ namespace tb {
 // norm.cu
 std::vector<at::Tensor> rms_norm_fwd(const at::Tensor& x, const at::Tensor& w, double eps);
 std::vector<at::Tensor> rms_norm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& w,
-                                     const at::Tensor& rstd, bool need_dw);
+                                     const at::Tensor& rstd, bool need_dw, const c10::optional<at::Tensor>& dadd);
+std::vector<at::Tensor> rms_norm_add_fwd(const at::Tensor& x, const at::Tensor& res, const at::Tensor& w, double eps);
 // conv.cu
 at::Tensor conv_silu_norm_fwd(const at::Tensor& x, const c10::optional<at::Tensor>& w,
                               const c10::optional<at::Tensor>& b, bool normalize);
@@ -76,7 +77,9 @@ void comm_adamw_shard(const at::Tensor& gsum, at::Tensor& master, at::Tensor& ex
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "titans_pytorch_b200 sm_100a kernels";
   m.def("rms_norm_fwd", &tb::rms_norm_fwd);
-  m.def("rms_norm_bwd", &tb::rms_norm_bwd);
+  m.def("rms_norm_bwd", &tb::rms_norm_bwd, pybind11::arg("dy"), pybind11::arg("x"), pybind11::arg("w"),
+        pybind11::arg("rstd"), pybind11::arg("need_dw"), pybind11::arg("dadd") = pybind11::none());
+  m.def("rms_norm_add_fwd", &tb::rms_norm_add_fwd);
   m.def("conv_silu_norm_fwd", &tb::conv_silu_norm_fwd);
   m.def("conv_silu_norm_bwd", &tb::conv_silu_norm_bwd);
   m.def("swiglu_fwd", &tb::swiglu_fwd);

@@ -16,7 +16,7 @@ template <typename T, int CH>
 __global__ void __launch_bounds__(256) rms_bwd_kernel(const T* __restrict__ dy, const T* __restrict__ x,
                                                       const T* __restrict__ w, const float* __restrict__ rstd,
                                                       T* __restrict__ dx, float* __restrict__ dw_part,
-                                                      int64_t rows, int D) {
+                                                      int64_t rows, int D, const T* __restrict__ dadd = nullptr) {
   constexpr int V = Vec16<T>::N;
   extern __shared__ float smem[];  // [nwarps][D]
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
@@ -59,6 +59,12 @@ __global__ void __launch_bounds__(256) rms_bwd_kernel(const T* __restrict__ dy, 
         for (int i = 0; i < V; ++i) {
           o[i] = rs * (a[i] * ww[i] - b[i] * dot);
           acc[c][i] += a[i] * b[i] * rs;
+        }
+        if (dadd != nullptr) {  // gradient arriving at the normalised input directly (fused residual add)
+          float e[V];
+          load16<T>(dadd + r * D + col, e);
+#pragma unroll
+          for (int i = 0; i < V; ++i) o[i] += e[i];
         }
         store16<T>(dxr + col, o);
       }

@@ -14,7 +14,7 @@ import torch.nn as nn
 
 from ..config import TitansConfig
 from ..ops.ffn import swiglu_ffn
-from ..ops.norm import rms_norm
+from ..ops.norm import fused_add_rms_norm, rms_norm
 
 
 class RMSNorm(nn.Module):
@@ -29,9 +29,8 @@ class RMSNorm(nn.Module):
         return rms_norm(x, self.weight, self.eps, self.use_kernels)
 
     def forward_with_residual(self, x: torch.Tensor, residual: torch.Tensor):
-        """(h, norm(h)) with h = x + residual."""
-        h = x + residual
-        return h, self(h)
+        """(h, norm(h)) with h = x + residual (one fused kernel on CUDA)."""
+        return fused_add_rms_norm(x, residual, self.weight, self.eps, self.use_kernels)
 
 
 class FeedForward(nn.Module):

@@ -105,9 +105,9 @@ class MALBlock(nn.Module):
 
     def forward(self, x: torch.Tensor, state: MemoryState | None = None, update_memory: bool = True):
         m, new_state = self.memory(self.norm1(x), state=state, update=update_memory)
-        x = x + self.dropout(m)
-        x = x + self.dropout(self.attention(self.norm2(x), prefix=self.persistent(x.shape[0])))
-        x = x + self.dropout(self.ffn(self.norm3(x)))
+        x, n2 = self.norm2.forward_with_residual(x, self.dropout(m))  # residual add fused with the norm
+        x, n3 = self.norm3.forward_with_residual(x, self.dropout(self.attention(n2, prefix=self.persistent(x.shape[0]))))
+        x = x + self.dropout(self.ffn(n3))
         return x, new_state
 
 
@@ -126,8 +126,8 @@ class LMMBlock(nn.Module):
 
     def forward(self, x: torch.Tensor, state: MemoryState | None = None, update_memory: bool = True):
         m, new_state = self.memory(self.norm1(x), state=state, update=update_memory)
-        x = x + self.dropout(m)
-        x = x + self.dropout(self.ffn(self.norm2(x)))
+        x, n2 = self.norm2.forward_with_residual(x, self.dropout(m))  # residual add fused with the norm
+        x = x + self.dropout(self.ffn(n2))
         return x, new_state
 
 

@@ -47,3 +47,45 @@ def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6,
     if want_kernels(x, use_kernels):
         return _RMSNormFn.apply(x, weight, eps)
     return rms_norm_reference(x, weight, eps)
+
+
+def fused_add_rms_norm_reference(x: torch.Tensor, residual: torch.Tensor, weight: torch.Tensor, eps: float):
+    hidden = x + residual
+    return hidden, rms_norm_reference(hidden, weight, eps)
+
+
+class _AddRMSNormFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, residual, weight, eps):
+        shape = x.shape
+        x2 = x.reshape(-1, shape[-1]).contiguous()
+        r2 = residual.reshape(-1, shape[-1]).to(x.dtype).contiguous()
+        h, y, rstd = ext().rms_norm_add_fwd(x2, r2, weight, float(eps))
+        ctx.save_for_backward(h, weight, rstd)
+        ctx.shape = shape
+        return h.view(shape), y.view(shape)
+
+    @staticmethod
+    def backward(ctx, dh, dy):
+        h, weight, rstd = ctx.saved_tensors
+        D = ctx.shape[-1]
+        dy2 = torch.zeros_like(h) if dy is None else dy.reshape(-1, D).contiguous()
+        dh2 = None if dh is None else dh.reshape(-1, D).to(h.dtype).contiguous()
+        dx, dw = ext().rms_norm_bwd(dy2, h, weight, rstd, ctx.needs_input_grad[2], dh2)
+        dw = dw.to(weight.dtype) if dw is not None and dw.numel() else None
+        dx = dx.view(ctx.shape)
+        return dx, dx, dw, None
+
+
+def fused_add_rms_norm(x: torch.Tensor, residual: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6,
+                       use_kernels: bool | None = None):
+    """``hidden = x + residual`` and ``rms_norm(hidden) * weight`` in one pass.
+
+    Returns ``(hidden, normalized)`` (the reference's
+    `cuda_optimizations.py:106-122` contract).  On CUDA one kernel reads both
+    inputs once and writes both outputs; the backward is one kernel that also
+    adds the gradient arriving at ``hidden``.
+    """
+    if want_kernels(x, use_kernels):
+        return _AddRMSNormFn.apply(x, residual, weight, eps)
+    return fused_add_rms_norm_reference(x, residual, weight, eps)

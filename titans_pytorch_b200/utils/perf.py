@@ -248,3 +248,90 @@ def is_flash_attention_available() -> bool:
 
 def is_torch_sdpa_available() -> bool:
     return hasattr(torch.nn.functional, "scaled_dot_product_attention")
+
+
+# ---------------------------------------------------------------- fused helpers and streams
+# (`src/titans/cuda_optimizations.py:37-148, 547-644` surface)
+from ..ops.norm import fused_add_rms_norm  # noqa: E402  (kernel-backed residual add + RMSNorm)
+
+
+def fused_silu_mul(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
+    """silu(gate) * up."""
+    return torch.nn.functional.silu(gate) * up
+
+
+def fused_linear_silu_linear(x: torch.Tensor, gate_weight: torch.Tensor, up_weight: torch.Tensor,
+                             down_weight: torch.Tensor) -> torch.Tensor:
+    """down(silu(x gate^T) * (x up^T)): the SwiGLU FFN (one stacked gate|up GEMM and
+    the SiLU-product kernel on CUDA)."""
+    from ..ops.ffn import swiglu_ffn
+
+    return swiglu_ffn(x, gate_weight, up_weight, down_weight)
+
+
+class CUDAStreamManager:
+    """A small pool of CUDA streams: ``with mgr.stream(i): ...`` runs work on
+    stream i; ``synchronize()`` joins every stream into the current one."""
+
+    def __init__(self, num_streams: int = 3) -> None:
+        self.enabled = torch.cuda.is_available()
+        self.streams = [torch.cuda.Stream() for _ in range(num_streams)] if self.enabled else []
+
+    @contextlib.contextmanager
+    def stream(self, stream_id: int = 0):
+        if not self.enabled:
+            yield None
+            return
+        s = self.streams[stream_id % len(self.streams)]
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            yield s
+
+    def synchronize(self) -> None:
+        if self.enabled:
+            cur = torch.cuda.current_stream()
+            for s in self.streams:
+                cur.wait_stream(s)
+
+
+@torch.no_grad()
+def optimized_generate_step(model, input_ids: torch.Tensor, states=None, context: int | None = None):
+    """One decoding step: logits of the next token for the last ``context``
+    tokens (default the model's chunk size) with the memory states carried.
+    Returns ``(next_logits [B, V], new_states)``."""
+    n = context or model.config.chunk_size
+    logits, states = model(input_ids[:, -min(n, input_ids.shape[1]):], states=states)
+    return logits[:, -1], states
+
+
+@torch.no_grad()
+def speculative_decode(model, draft_model, input_ids: torch.Tensor, num_speculative_tokens: int = 4,
+                       max_new_tokens: int = 32, context: int | None = None) -> torch.Tensor:
+    """Greedy speculative decoding over a sliding context window.
+
+    The draft model proposes ``num_speculative_tokens`` tokens greedily; the
+    target scores the window plus all proposals in ONE forward and keeps the
+    longest prefix it agrees with, plus its own next token.  Neither model
+    carries memory states.  When a model's output at a position depends only on
+    its last ``context`` tokens, the result equals plain greedy decoding with that
+    window. That holds for MAG / MAL / LMM with an attention window no larger than
+    ``context``: without carried states the memory is read at its initial weights
+    per position. It does not hold for MAC, whose segment memory tokens depend on
+    the whole segment.
+    """
+    n = context or model.config.chunk_size
+    out = input_ids
+    while out.shape[1] - input_ids.shape[1] < max_new_tokens:
+        draft = out
+        for _ in range(num_speculative_tokens):
+            lg, _ = draft_model(draft[:, -n:])
+            draft = torch.cat([draft, lg[:, -1:].argmax(-1)], 1)
+        k = draft.shape[1] - out.shape[1]
+        span = draft[:, -(n + k):]
+        lg, _ = model(span)
+        choice = lg[:, -(k + 1):].argmax(-1)          # target's token after each proposal prefix
+        proposed = draft[:, out.shape[1]:]
+        agree = (choice[:, :k] == proposed).all(0)    # accept a position only if every row agrees
+        m = int(agree.int().cumprod(0).sum())
+        out = torch.cat([out, proposed[:, :m], choice[:, m:m + 1]], 1)
+    return out[:, :input_ids.shape[1] + max_new_tokens]

@@ -234,19 +234,34 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       const int lo2 = max(pre_hi, P - n0 + win_lo);
       const int hi2 = min(BN, P - n0 + win_hi + 1);
       const bool row_full = (pre_hi >= BN) || (lo2 <= pre_hi && pre_hi == 0 && lo2 <= 0 && hi2 >= BN);
+      const bool warp_full = __all_sync(0xffffffffu, row_full);
+      // 32-column chunks that some row of this warp can see (bit c); the others
+      // (beyond the diagonal, before the window, the non-prefix part of the
+      // prefix tile) skip the max and the exponentials and store P = 0
+      unsigned vis_chunks = 0;
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c) {
+        const int a = c * 32;
+        if (__any_sync(0xffffffffu, (a < pre_hi) || (a < hi2 && a + 32 > lo2))) vis_chunks |= 1u << c;
+      }
       float mx[8];
 #pragma unroll
       for (int k = 0; k < 8; ++k) mx[k] = -INFINITY;
-      if (__all_sync(0xffffffffu, row_full)) {
+      if (warp_full) {
         // every row of this warp sees the whole tile: no masking
 #pragma unroll
         for (int c = 0; c < BN; ++c) mx[c & 7] = fmaxf(mx[c & 7], s[c]);
       } else {
 #pragma unroll
-        for (int c = 0; c < BN; ++c) {
-          const bool vis = (c < pre_hi) | ((c >= lo2) & (c < hi2));
-          s[c] = vis ? s[c] : -INFINITY;
-          mx[c & 7] = fmaxf(mx[c & 7], s[c]);
+        for (int cc = 0; cc < BN / 32; ++cc) {
+          if (!((vis_chunks >> cc) & 1u)) continue;
+#pragma unroll
+          for (int x = 0; x < 32; ++x) {
+            const int c = cc * 32 + x;
+            const bool vis = (c < pre_hi) | ((c >= lo2) & (c < hi2));
+            s[c] = vis ? s[c] : -INFINITY;
+            mx[x & 7] = fmaxf(mx[x & 7], s[c]);
+          }
         }
       }
       // raw-score max; the softmax scale (> 0) is folded into one FFMA before ex2
@@ -266,12 +281,17 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 #pragma unroll
       for (int c = 0; c < BN; c += 32) {
         uint32_t pk[16];
+        if ((vis_chunks >> (c >> 5)) & 1u) {
 #pragma unroll
-        for (int x = 0; x < 32; x += 2) {
-          const float p0 = ex2(fmaf(s[c + x], scale_log2, -m_use));
-          const float p1 = ex2(fmaf(s[c + x + 1], scale_log2, -m_use));
-          sm[(x >> 1) & 7] += p0 + p1;
-          pk[x >> 1] = pack2(p0, p1);
+          for (int x = 0; x < 32; x += 2) {
+            const float p0 = ex2(fmaf(s[c + x], scale_log2, -m_use));
+            const float p1 = ex2(fmaf(s[c + x + 1], scale_log2, -m_use));
+            sm[(x >> 1) & 7] += p0 + p1;
+            pk[x >> 1] = pack2(p0, p1);
+          }
+        } else {
+#pragma unroll
+          for (int x = 0; x < 16; ++x) pk[x] = 0u;
         }
         uint8_t* blk = sP + (c >> 6) * (BM * 128) + row * 128;
 #pragma unroll
@@ -768,6 +788,13 @@ __global__ void __launch_bounds__(320, 1)
 #pragma unroll
       for (int cc = 0; cc < 2; ++cc) {
         const int c = wg * 2 + cc;  // 32-query chunk handled by this warpgroup
+        // no key row of this warp sees a query of the chunk (beyond the window, or
+        // the non-prefix rows of the prefix tile): P^T = dS^T = 0 without the math
+        if (!__any_sync(0xffffffffu, c_lo < c * 32 + 32 && c_hi > c * 32)) {
+#pragma unroll
+          for (int x = 0; x < 16; ++x) pp[cc * 16 + x] = dd[cc * 16 + x] = 0u;
+          continue;
+        }
         uint32_t st[32], dp[32];
         tc::tmem_ld32(tl + TM_ST + c * 32, st);
         tc::tmem_ld32(tl + TM_DPT + c * 32, dp);

@@ -23,7 +23,7 @@ import statistics
 import torch
 
 OPS = ("attn_fwd_tc", "attn_fwd_mma", "attn_bwd_tc", "attn_bwd_mma", "conv_fwd", "conv_bwd", "rms_fwd",
-       "rms_bwd", "swiglu_fwd", "swiglu_bwd", "ce_fwd")
+       "rms_bwd", "swiglu_fwd", "swiglu_bwd", "ce_fwd", "gemm_tc", "gemm_cublas", "gemm_gather")
 
 
 def visible_pairs(T: int, W: int, P: int) -> int:
@@ -100,6 +100,21 @@ def build(op: str, a) -> tuple:
         logits = rn(rows, a.vocab)
         labels = torch.randint(0, a.vocab, (rows,), device=dev, generator=g)
         return (lambda: E.cross_entropy_fwd(logits, labels, -100)), 0, logits.numel() * 2
+    if op.startswith("gemm"):
+        # the first projection of a layer: [B*T, D] x [3D, D]^T (q|k|v)
+        M, N, K = rows, a.gemm_n or 3 * D, D
+        x, w = rn(M, K), rn(N, K)
+        flops = 2.0 * M * N * K
+        if op == "gemm_tc":
+            return (lambda: E.gemm_tc(x, w)), flops, 0
+        if op == "gemm_cublas":
+            return (lambda: torch.matmul(x, w.t())), flops, 0
+        # fused prefetch of a 16M-parameter layer gathered from 8 emulated owners on this GPU
+        unit = 16 << 20
+        bufs = [rn(unit) for _ in range(8)]
+        ptrs = torch.tensor([t.data_ptr() for t in bufs], dtype=torch.int64, device=dev)
+        shard = unit // 8
+        return (lambda: E.gemm_gather_tc(x, w, bufs[0], ptrs, 0, unit, shard, 0, False)), flops, 0
     raise ValueError(op)
 
 
@@ -115,6 +130,7 @@ def main(argv=None) -> None:
     add("--persistent", type=int, default=4)
     add("--ffn-mult", type=float, default=4.0)
     add("--vocab", type=int, default=32000)
+    add("--gemm-n", type=int, default=0, help="GEMM N (default 3 x heads x head_dim)")
     add("--warmup", type=int, default=3)
     add("--iters", type=int, default=10)
     add("--no-flush", action="store_true")

@@ -71,7 +71,14 @@ void comm_adamw_shard(const at::Tensor& gsum, at::Tensor& master, at::Tensor& ex
                       const at::Tensor& param_ptrs, int64_t lo, int64_t world, const at::Tensor& tab, int64_t nseg,
                       int64_t items, const at::Tensor& norm_slots, double gscale, double max_norm, double lr,
                       double beta1, double beta2, double eps, double wd, int64_t step, at::Tensor& norm_out,
-                      const c10::optional<at::Tensor>& hyper);
+                      const c10::optional<at::Tensor>& hyper, const c10::optional<at::Tensor>& seg_aux, int64_t me);
+void comm_reduce_segments(const at::Tensor& grad_ptrs, const at::Tensor& tab, int64_t nseg, int64_t items,
+                          at::Tensor& gsum, double gscale, const at::Tensor& slot_ptrs, int64_t world, int64_t me);
+// gemm_tc.cu
+at::Tensor gemm_tc(const at::Tensor& A, const at::Tensor& B);
+at::Tensor gemm_gather_tc(const at::Tensor& A, const at::Tensor& B, at::Tensor& flat, const at::Tensor& src_ptrs,
+                          int64_t u0, int64_t len, int64_t shard, int64_t me, bool consume);
+void fsdp_gather(at::Tensor& flat, const at::Tensor& src_ptrs, int64_t u0, int64_t len, int64_t shard, int64_t me);
 }  // namespace tb
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -111,6 +118,16 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("comm_ipc_close", &tb::comm_ipc_close);
   m.def("comm_barrier", &tb::comm_barrier);
   m.def("comm_reduce_shard", &tb::comm_reduce_shard);
-  m.def("comm_adamw_shard", &tb::comm_adamw_shard);
+  m.def("comm_adamw_shard", &tb::comm_adamw_shard, pybind11::arg("gsum"), pybind11::arg("master"),
+        pybind11::arg("exp_avg"), pybind11::arg("exp_avg_sq"), pybind11::arg("param_ptrs"), pybind11::arg("lo"),
+        pybind11::arg("world"), pybind11::arg("tab"), pybind11::arg("nseg"), pybind11::arg("items"),
+        pybind11::arg("norm_slots"), pybind11::arg("gscale"), pybind11::arg("max_norm"), pybind11::arg("lr"),
+        pybind11::arg("beta1"), pybind11::arg("beta2"), pybind11::arg("eps"), pybind11::arg("wd"),
+        pybind11::arg("step"), pybind11::arg("norm_out"), pybind11::arg("hyper") = pybind11::none(),
+        pybind11::arg("seg_aux") = pybind11::none(), pybind11::arg("me") = 0);
+  m.def("comm_reduce_segments", &tb::comm_reduce_segments);
+  m.def("gemm_tc", &tb::gemm_tc);
+  m.def("gemm_gather_tc", &tb::gemm_gather_tc);
+  m.def("fsdp_gather", &tb::fsdp_gather);
   m.def("kernel_error_status", &tb::kernel_error_status, pybind11::arg("device") = 0, pybind11::arg("reset") = true);
 }

@@ -87,6 +87,14 @@ __global__ void reduce_shard_kernel(const __nv_bfloat16* const* __restrict__ gra
   if (threadIdx.x == 0) part[blockIdx.x] = acc;
 }
 
+// Segment form (sharded-parameter layout): for segment s = (flat offset,
+// shard offset, length), g[shard_off + i] = sum_r G_r[flat_off + i]; work
+// items are kChunk-element pieces of the segments.
+__global__ void reduce_segments_kernel(const __nv_bfloat16* const* __restrict__ grads,
+                                       const int64_t* __restrict__ segs, const int64_t* __restrict__ item_start,
+                                       int nseg, int64_t nitems, int world, float* __restrict__ gsum, float gscale,
+                                       float* __restrict__ part);
+
 // single block: slot[me] of every peer <- sum(part)
 __global__ void norm_publish_kernel(const float* __restrict__ part, int nparts, float* const* __restrict__ slots,
                                     int world, int me) {
@@ -116,14 +124,48 @@ __device__ __forceinline__ int find_seg(const int64_t* __restrict__ item_start, 
   return lo;
 }
 
+__global__ void reduce_segments_kernel(const __nv_bfloat16* const* __restrict__ grads,
+                                       const int64_t* __restrict__ segs, const int64_t* __restrict__ item_start,
+                                       int nseg, int64_t nitems, int world, float* __restrict__ gsum, float gscale,
+                                       float* __restrict__ part) {
+  __shared__ float red[32];
+  float acc = 0.f;
+  for (int64_t it = blockIdx.x; it < nitems; it += gridDim.x) {
+    const int s = find_seg(item_start, nseg, it);
+    const int64_t foff = segs[3 * s], soff = segs[3 * s + 1], len = segs[3 * s + 2];
+    const int64_t c0 = (it - item_start[s]) * kChunk, c1 = min(len, c0 + kChunk);
+    for (int64_t e = c0 + threadIdx.x * 8; e < c1; e += blockDim.x * 8) {
+      float sum[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      for (int r = 0; r < world; ++r) {
+        float x[8];
+        load16<__nv_bfloat16>(grads[r] + foff + e, x);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) sum[k] += x[k];
+      }
+      float4* dst = reinterpret_cast<float4*>(gsum + soff + e);
+      dst[0] = make_float4(sum[0], sum[1], sum[2], sum[3]);
+      dst[1] = make_float4(sum[4], sum[5], sum[6], sum[7]);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) acc += (sum[k] * gscale) * (sum[k] * gscale);
+    }
+  }
+  acc = block_sum(acc, red);
+  if (threadIdx.x == 0) part[blockIdx.x] = acc;
+}
+
 // AdamW on the shard's active ranges (shard-relative offsets, multiples of 8),
 // new bf16 weights stored into every rank's parameter buffer at lo + i.
+// With `seg_aux` (sharded-parameter layout) segment s is stored at
+// lo + i + seg_aux[2s] instead, into every rank's buffer when seg_aux[2s+1]
+// is nonzero (replicated parameters) and into this rank's only otherwise
+// (sharded parameters, gathered by the next forward).
 __global__ void adamw_shard_kernel(const float* __restrict__ gsum, float* __restrict__ master, float* __restrict__ m,
                                    float* __restrict__ v, __nv_bfloat16* const* __restrict__ params, int64_t lo,
                                    int world, const int64_t* __restrict__ segs, const int64_t* __restrict__ item_start,
                                    int nseg, int64_t nitems, const float* __restrict__ norm_slots, float gscale,
                                    float max_norm, float lr, float b1, float b2, float eps, float wd, float bc1,
-                                   float bc2_sqrt, float* __restrict__ norm_out, const float* __restrict__ hyper) {
+                                   float bc2_sqrt, float* __restrict__ norm_out, const float* __restrict__ hyper,
+                                   const int64_t* __restrict__ seg_aux, int me) {
   if (hyper) {  // [step, lr, bc1, sqrt(bc2)] advanced on the device (CUDA-graph replay)
     lr = hyper[1];
     bc1 = hyper[2];
@@ -140,6 +182,8 @@ __global__ void adamw_shard_kernel(const float* __restrict__ gsum, float* __rest
     const int64_t off = segs[2 * s], len = segs[2 * s + 1];
     const int64_t c0 = (it - item_start[s]) * kChunk;
     const int64_t c1 = min(len, c0 + kChunk);
+    const int64_t delta = seg_aux ? seg_aux[2 * s] : 0;
+    const bool all_ranks = seg_aux ? seg_aux[2 * s + 1] != 0 : true;
     for (int64_t e = off + c0 + threadIdx.x * 8; e < off + c1; e += blockDim.x * 8) {
       float g8[8], p8[8], m8[8], v8[8], out[8];
       load8f(gsum + e, g8);
@@ -160,7 +204,11 @@ __global__ void adamw_shard_kernel(const float* __restrict__ gsum, float* __rest
       Vec16<__nv_bfloat16> pk;
 #pragma unroll
       for (int k = 0; k < 8; ++k) pk.v[k] = __float2bfloat16_rn(out[k]);
-      for (int r = 0; r < world; ++r) *reinterpret_cast<uint4*>(params[r] + lo + e) = pk.raw;
+      if (all_ranks) {
+        for (int r = 0; r < world; ++r) *reinterpret_cast<uint4*>(params[r] + lo + e + delta) = pk.raw;
+      } else {
+        *reinterpret_cast<uint4*>(params[me] + lo + e + delta) = pk.raw;
+      }
     }
   }
   __threadfence_system();
@@ -232,7 +280,7 @@ void comm_adamw_shard(const at::Tensor& gsum, at::Tensor& master, at::Tensor& ex
                       const at::Tensor& param_ptrs, int64_t lo, int64_t world, const at::Tensor& tab, int64_t nseg,
                       int64_t items, const at::Tensor& norm_slots, double gscale, double max_norm, double lr,
                       double beta1, double beta2, double eps, double wd, int64_t step, at::Tensor& norm_out,
-                      const c10::optional<at::Tensor>& hyper) {
+                      const c10::optional<at::Tensor>& hyper, const c10::optional<at::Tensor>& seg_aux, int64_t me) {
   if (nseg == 0) return;
   const int64_t* segs = tab.data_ptr<int64_t>();
   const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>(items, num_sms() * 8));
@@ -243,8 +291,29 @@ void comm_adamw_shard(const at::Tensor& gsum, at::Tensor& master, at::Tensor& ex
       reinterpret_cast<__nv_bfloat16* const*>(param_ptrs.data_ptr<int64_t>()), lo, (int)world, segs,
       segs + 2 * nseg, (int)nseg, items, norm_slots.data_ptr<float>(), (float)gscale, (float)max_norm, (float)lr,
       (float)beta1, (float)beta2, (float)eps, (float)wd, bc1, bc2s, norm_out.data_ptr<float>(),
-      (hyper.has_value() && hyper->defined()) ? hyper->data_ptr<float>() : nullptr);
+      (hyper.has_value() && hyper->defined()) ? hyper->data_ptr<float>() : nullptr,
+      (seg_aux.has_value() && seg_aux->defined()) ? seg_aux->data_ptr<int64_t>() : nullptr, (int)me);
   check_launch("comm_adamw_shard");
+}
+
+// Reduce-scatter in the sharded-parameter layout: `tab` = [nseg][3] (flat
+// offset, shard offset, length; multiples of 8) followed by the segments'
+// first work-item indices; then the shard's squared norm is published into
+// every peer's slot array.
+void comm_reduce_segments(const at::Tensor& grad_ptrs, const at::Tensor& tab, int64_t nseg, int64_t items,
+                          at::Tensor& gsum, double gscale, const at::Tensor& slot_ptrs, int64_t world, int64_t me) {
+  const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>(items, num_sms() * 8));
+  at::Tensor part = at::zeros({blocks}, gsum.options());
+  if (nseg > 0) {
+    const int64_t* segs = tab.data_ptr<int64_t>();
+    comm::reduce_segments_kernel<<<blocks, 256, 0, stream()>>>(
+        reinterpret_cast<const __nv_bfloat16* const*>(grad_ptrs.data_ptr<int64_t>()), segs, segs + 3 * nseg,
+        (int)nseg, items, (int)world, gsum.data_ptr<float>(), (float)gscale, part.data_ptr<float>());
+  }
+  comm::norm_publish_kernel<<<1, 256, 0, stream()>>>(part.data_ptr<float>(), blocks,
+                                                     reinterpret_cast<float* const*>(slot_ptrs.data_ptr<int64_t>()),
+                                                     (int)world, (int)me);
+  check_launch("comm_reduce_segments");
 }
 
 }  // namespace tb

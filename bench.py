@@ -206,7 +206,7 @@ def count_launches(step_fn, prefixes) -> tuple[int, int]:
 
 
 # ---------------------------------------------------------------------------- arms
-def build_ours(device, world):
+def build_ours(device, world, parallel="dp"):
     from titans_pytorch_b200 import TitansConfig, create_model
     from titans_pytorch_b200.train.trainer import Trainer, TrainStepConfig
     from titans_pytorch_b200.utils.perf import enable_gradient_checkpointing
@@ -216,7 +216,11 @@ def build_ours(device, world):
     if CFG["ckpt"]:
         enable_gradient_checkpointing(model)
     engine = None
-    if world > 1:
+    if world > 1 and parallel == "fsdp":
+        from titans_pytorch_b200.parallel.fsdp import FullyShardedEngine
+
+        engine = FullyShardedEngine()
+    elif world > 1:
         from titans_pytorch_b200.parallel.ddp import DataParallelEngine
 
         engine = DataParallelEngine()
@@ -297,6 +301,9 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--config", choices=sorted(CONFIGS), default="mag170m")
+    ap.add_argument("--parallel", choices=["dp", "fsdp"], default="dp",
+                    help="N > 1, this framework: dp = replicated weights, optimizer state sharded; fsdp = "
+                         "parameters sharded per block, all-gathered inside the first GEMM of the previous block")
     args = ap.parse_args()
     global CFG, MODEL_FIELDS, SEQ, MICRO_BATCH
     CFG = CONFIGS[args.config]
@@ -319,7 +326,7 @@ def main():
         trainer, nparams = built
         prefixes = ()
     else:
-        trainer, nparams = build_ours(device, world)
+        trainer, nparams = build_ours(device, world, args.parallel)
         prefixes = ("tb::",)
 
     batches = make_batches(world, rank, W + K + 1)
@@ -377,6 +384,9 @@ def main():
     parallelism = f"dp{world}"
     if world > 1:
         parallelism = (f"dp{world} (grads all-reduced after backward)" if args.impl == "reference"
+                       else f"fsdp{world} (per-block parameter shards; all-gather fused into the previous "
+                            f"block's first tcgen05 GEMM; fused reduce-scatter / AdamW shard)"
+                       if args.parallel == "fsdp"
                        else f"dp{world} (fused reduce-scatter / AdamW shard / all-gather)")
     if rank == 0:
         out = {

@@ -11,6 +11,12 @@ take the in-place path when their ``.grad`` tensors are adjacent in one buffer,
 as :class:`~titans_pytorch_b200.train.optim.FlatParamSpace` lays them out. In
 every other case, and always outside the context, the gradients go back
 to autograd as usual (``torch.autograd.grad`` included).
+
+:func:`set_prefetch` installs a one-shot forward hook used by the sharded
+data-parallel engine: the next ``linear`` call hands its GEMM to the hook
+(which runs it on the kernel that also all-gathers the next block's
+parameters) and the hook is dropped.  A hook that returns None leaves the
+GEMM to cuBLAS and stays installed.
 """
 
 from __future__ import annotations
@@ -20,7 +26,22 @@ import contextlib
 import torch
 import torch.nn.functional as F
 
-_STATE = {"inplace": False}
+_STATE = {"inplace": False, "prefetch": None}
+
+
+def set_prefetch(fn) -> None:
+    """Install (or clear, with None) the one-shot GEMM hook ``fn(x, w) -> y | None``."""
+    _STATE["prefetch"] = fn
+
+
+def _mm(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    fn = _STATE["prefetch"]
+    if fn is not None:
+        y = fn(x, w)
+        if y is not None:
+            _STATE["prefetch"] = None
+            return y
+    return F.linear(x, w)
 
 
 @contextlib.contextmanager
@@ -56,7 +77,7 @@ class _Linear(torch.autograd.Function):
         w = weights[0] if n == 1 else torch.cat(weights, 0)
         ctx.save_for_backward(x, w)
         ctx.weights = weights
-        return F.linear(x, w)
+        return _mm(x, w)
 
     @staticmethod
     def backward(ctx, dy):
@@ -85,8 +106,8 @@ def linear(x: torch.Tensor, *weights: torch.Tensor) -> torch.Tensor:
     """``x @ cat(weights)^T`` (no bias)."""
     if not torch.is_grad_enabled() or not any(w.requires_grad for w in weights):
         w = weights[0] if len(weights) == 1 else torch.cat(weights, 0)
-        return F.linear(x, w)
+        return _mm(x, w)
     return _Linear.apply(x, len(weights), *weights)
 
 
-__all__ = ["linear", "accumulate_weight_grads"]
+__all__ = ["linear", "accumulate_weight_grads", "set_prefetch"]

@@ -58,6 +58,9 @@ def build_parser() -> argparse.ArgumentParser:
     a("--weight-decay", type=float, default=0.1)
     a("--grad-clip", type=float, default=1.0)
     a("--warmup-ratio", type=float, default=0.03)
+    a("--parallel", choices=["dp", "fsdp"], default="dp",
+      help="under torchrun: dp = replicated weights with the optimizer state sharded; fsdp = parameters "
+           "sharded per block, all-gathered in the forward")
     a("--mixed-precision", choices=["none", "fp16", "bf16"], default="bf16")
     a("--checkpoint-dir", type=str, default="checkpoints")
     a("--save-every", type=int, default=1000)
@@ -90,6 +93,13 @@ def build_dataset(args, vocab_size):
     return SyntheticDataset(vocab_size, args.seq_len, args.synthetic_samples, seed=args.seed)
 
 
+def _full_params(tr) -> None:
+    """Every rank: gather parameters that are still sharded (FSDP) before rank 0 reads them."""
+    mat = getattr(tr.optimizer, "materialize", None)
+    if mat is not None:
+        mat()
+
+
 def main(argv=None) -> None:
     args = build_parser().parse_args(argv)
     logging.basicConfig(level=logging.INFO, format="%(asctime)s %(levelname)s %(message)s")
@@ -104,10 +114,11 @@ def main(argv=None) -> None:
         import torch.distributed as dist
 
         from ..parallel.ddp import DataParallelEngine
+        from ..parallel.fsdp import FullyShardedEngine
 
         dist.init_process_group("nccl" if device.type == "cuda" else "gloo",
                                 timeout=datetime.timedelta(seconds=600))
-        engine = DataParallelEngine()
+        engine = FullyShardedEngine() if args.parallel == "fsdp" else DataParallelEngine()
     torch.manual_seed(args.seed)
     fields = dict(dim=args.dim, num_heads=args.num_heads, num_layers=args.num_layers, vocab_size=args.vocab_size,
                   chunk_size=args.chunk_size, window_size=args.window_size,
@@ -168,6 +179,9 @@ def main(argv=None) -> None:
                             f.write(json.dumps(m) + "\n")
                     if wb is not None:
                         wb.log(m, step=tr.global_step)
+            if args.save_every > 0 and tr.global_step and tr.global_step % args.save_every == 0 \
+                    and tr._micro % args.gradient_accumulation_steps == 0:
+                _full_params(tr)
             if rank == 0 and args.save_every > 0 and tr.global_step and tr.global_step % args.save_every == 0 \
                     and tr._micro % args.gradient_accumulation_steps == 0:
                 save_checkpoint(os.path.join(args.checkpoint_dir, f"step_{tr.global_step}.pt"), tr.model,
@@ -178,6 +192,7 @@ def main(argv=None) -> None:
                 break
         if done:
             break
+    _full_params(tr)
     if rank == 0:
         save_checkpoint(os.path.join(args.checkpoint_dir, "final_model.pt"), tr.model, tr.optimizer, tr.scheduler,
                         global_step=tr.global_step, model_type=args.model, tokenizer_name=args.tokenizer,

@@ -11,6 +11,7 @@
 //               overlaps the next tile's MMAs
 //   warps 2-5   epilogue: thread = accumulator row (TMEM lane), tcgen05.ld of
 //               32 columns at a time, bf16 conversion, 64-byte row stores
+//               (8 warps splitting the columns measured slower)
 //   warp 6      gather (fused mode only)
 //
 // Fused all-gather.  The parameters of a unit (flat elements [u0, u0 + len)
@@ -51,7 +52,9 @@ constexpr int PIECE_BYTES = PIECE * 2;
 constexpr int OFF_G = NS * STAGE;
 constexpr int OFF_BAR = OFF_G + 2 * PIECE_BYTES;
 constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;  // barriers + alignment slack
-constexpr int NTHREADS = 224;
+constexpr int EPI_WARPS = 4;  // a multiple of 4 (one warp per TMEM lane quarter and column slice)
+constexpr int EPI_CHUNKS = BN / 32 / (EPI_WARPS / 4);  // 32-column chunks per epilogue warp
+constexpr int NTHREADS = 32 * (3 + EPI_WARPS);
 constexpr int TM_COLS = 2 * BN;
 
 enum : unsigned { ERR_GATHER_WAIT = 40 };
@@ -120,7 +123,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
     for (int b = 0; b < 2; ++b) {
       tc::mbar_init(bar_acc_full + b, 1);
-      tc::mbar_init(bar_acc_empty + b, 128);
+      tc::mbar_init(bar_acc_empty + b, 32 * EPI_WARPS);
       tc::mbar_init(bar_g + b, 1);
     }
     *abort_flag = 0;
@@ -207,9 +210,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         if (ok) tc::umma_commit(bar_acc_full + buf);
       }
     }
-  } else if (warp <= 5) {
+  } else if (warp < 2 + EPI_WARPS) {
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int slice = (warp - 2) >> 2;  // column slice of the tile
     const int r_in = q * 32 + lane;
     int li = 0;
     for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++li) {
@@ -220,7 +224,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       const int row = mt * BM + r_in;
       __nv_bfloat16* crow = C + (int64_t)row * N + nt * BN;
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
+      for (int c = slice * EPI_CHUNKS; c < (slice + 1) * EPI_CHUNKS; ++c) {
         const int col0 = nt * BN + c * 32;
         if (col0 >= N) break;  // warp-uniform
         uint32_t r[32];

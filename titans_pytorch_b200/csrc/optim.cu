@@ -7,6 +7,8 @@
 // `segs` is a device int64 [nseg, 2] table of (offset, length) ranges that
 // received a gradient this step; parameters outside it are left untouched,
 // matching torch.optim.AdamW's skip of parameters whose .grad is None.
+// Offsets and lengths are multiples of 8 (parameters are padded to 64
+// elements), so every thread moves 8 elements with 16/32-byte accesses.
 #include "common.cuh"
 
 namespace tb {
@@ -24,6 +26,26 @@ __device__ __forceinline__ int find_seg(const int64_t* __restrict__ item_start, 
   return lo;
 }
 
+// 8 consecutive elements as fp32 (16-byte bf16 or 2 x 16-byte fp32 accesses)
+template <typename T>
+__device__ __forceinline__ void ld8(const T* __restrict__ p, float (&o)[8]) {
+  if constexpr (std::is_same<T, float>::value) {
+    const float4 a = *reinterpret_cast<const float4*>(p), b = *reinterpret_cast<const float4*>(p + 4);
+    o[0] = a.x; o[1] = a.y; o[2] = a.z; o[3] = a.w; o[4] = b.x; o[5] = b.y; o[6] = b.z; o[7] = b.w;
+  } else {
+    load16<T>(p, o);
+  }
+}
+template <typename T>
+__device__ __forceinline__ void st8(T* __restrict__ p, const float (&o)[8]) {
+  if constexpr (std::is_same<T, float>::value) {
+    *reinterpret_cast<float4*>(p) = make_float4(o[0], o[1], o[2], o[3]);
+    *reinterpret_cast<float4*>(p + 4) = make_float4(o[4], o[5], o[6], o[7]);
+  } else {
+    store16<T>(p, o);
+  }
+}
+
 template <typename G>
 __global__ void sumsq_kernel(const G* __restrict__ g, const int64_t* __restrict__ segs,
                              const int64_t* __restrict__ item_start, int nseg, int64_t nitems, float scale,
@@ -35,9 +57,11 @@ __global__ void sumsq_kernel(const G* __restrict__ g, const int64_t* __restrict_
     const int64_t off = segs[2 * s], len = segs[2 * s + 1];
     const int64_t c0 = (it - item_start[s]) * kChunk;
     const int64_t c1 = min(len, c0 + kChunk);
-    for (int64_t i = c0 + threadIdx.x; i < c1; i += blockDim.x) {
-      const float v = to_f<G>(g[off + i]) * scale;
-      acc += v * v;
+    for (int64_t i = c0 + threadIdx.x * 8; i < c1; i += blockDim.x * 8) {
+      float x[8];
+      ld8<G>(g + off + i, x);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) acc += (x[k] * scale) * (x[k] * scale);
     }
   }
   acc = block_sum(acc, red);
@@ -76,16 +100,23 @@ __global__ void adamw_kernel(float* __restrict__ master, float* __restrict__ m, 
     const int64_t off = segs[2 * s], len = segs[2 * s + 1];
     const int64_t c0 = (it - item_start[s]) * kChunk;
     const int64_t c1 = min(len, c0 + kChunk);
-    for (int64_t i = off + c0 + threadIdx.x; i < off + c1; i += blockDim.x) {
-      const float gr = to_f<G>(g[i]) * cg;
-      float p = master[i] * decay;
-      const float mi = b1 * m[i] + (1.f - b1) * gr;
-      const float vi = b2 * v[i] + (1.f - b2) * gr * gr;
-      m[i] = mi;
-      v[i] = vi;
-      p -= step * mi / (sqrtf(vi) / bc2_sqrt + eps);
-      master[i] = p;
-      if (pout) pout[i] = from_f<P>(p);
+    for (int64_t i = off + c0 + threadIdx.x * 8; i < off + c1; i += blockDim.x * 8) {
+      float g8[8], p8[8], m8[8], v8[8];
+      ld8<G>(g + i, g8);
+      ld8<float>(master + i, p8);
+      ld8<float>(m + i, m8);
+      ld8<float>(v + i, v8);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const float gr = g8[k] * cg;
+        m8[k] = b1 * m8[k] + (1.f - b1) * gr;
+        v8[k] = b2 * v8[k] + (1.f - b2) * gr * gr;
+        p8[k] = p8[k] * decay - step * m8[k] / (sqrtf(v8[k]) / bc2_sqrt + eps);
+      }
+      st8<float>(m + i, m8);
+      st8<float>(v + i, v8);
+      st8<float>(master + i, p8);
+      if (pout) st8<P>(pout + i, p8);
     }
   }
 }

@@ -121,6 +121,8 @@ class FlatParamSpace:
 def segment_table(segs: list[tuple[int, int]], device, chunk: int = 1 << 14):
     """Device table consumed by the optimizer kernels: offsets, lengths, item starts."""
     n = len(segs)
+    if any(o % 8 or ln % 8 for o, ln in segs):
+        raise ValueError("optimizer segments must be 8-element aligned (the kernels move 8 elements per access)")
     tab = torch.empty(3 * n, dtype=torch.long)
     items = 0
     for i, (o, ln) in enumerate(segs):

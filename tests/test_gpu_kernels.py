@@ -51,7 +51,7 @@ def test_rms_norm(rows, D, dtype):
     assert rel_err(w.grad, wr.grad) < tol
 
 
-@pytest.mark.parametrize("B,T,D", [(2, 37, 64), (3, 129, 768), (1, 5, 128)])
+@pytest.mark.parametrize("B,T,D", [(2, 37, 64), (3, 129, 768), (1, 5, 128), (2, 64, 768), (1, 12, 1536), (3, 8, 64)])
 @pytest.mark.parametrize("normalize", [True, False])
 @pytest.mark.parametrize("conv", [True, False])
 def test_conv_silu_norm(B, T, D, normalize, conv):

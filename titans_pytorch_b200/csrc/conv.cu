@@ -129,6 +129,82 @@ __global__ void __launch_bounds__(512) conv_fwd_rows(const T* __restrict__ x, in
   }
 }
 
+// R consecutive tokens of one sequence per thread (Tn % R == 0): the R + KS - 1
+// input rows are loaded once (instead of KS times each), the taps and the bias
+// once per thread, and the R row norms share one block reduction.
+template <typename T, int KS, int R>
+__global__ void __launch_bounds__(256) conv_fwd_rrows(const T* __restrict__ x, int64_t sb, int64_t st,
+                                                      const T* __restrict__ wt, const T* __restrict__ bias,
+                                                      T* __restrict__ y, int64_t rows, int Tn, int D, bool normalize) {
+  constexpr int V = Vec16<T>::N;
+  __shared__ float red[8][R][8];  // [row group][row][warp of the row]
+  const int nw = blockDim.x >> 5, lane = threadIdx.x & 31, wir = threadIdx.x >> 5;
+  const int64_t r0 = ((int64_t)blockIdx.x * blockDim.y + threadIdx.y) * R;
+  const int col = threadIdx.x * V;
+  const bool active = col < D && r0 < rows;
+  float o[R][V];
+  float ss[R];
+#pragma unroll
+  for (int k = 0; k < R; ++k) ss[k] = 0.f;
+  if (active) {
+    const int b = (int)(r0 / Tn), t0 = (int)(r0 % Tn);
+    const T* xb = x + (int64_t)b * sb + col;
+    float xin[R + KS - 1][V];  // xin[i] = x[t0 - KS + 1 + i]
+#pragma unroll
+    for (int i = 0; i < R + KS - 1; ++i) {
+      const int tt = t0 - KS + 1 + i;
+      load16<T>(xb + (int64_t)max(tt, 0) * st, xin[i]);
+      if (tt < 0)
+#pragma unroll
+        for (int e = 0; e < V; ++e) xin[i][e] = 0.f;
+    }
+    float bv[V];
+    load_bias<T>(bias, col, bv);
+    float wj[KS][V];
+    if (wt) load_taps<T, KS>(wt, col, wj);
+#pragma unroll
+    for (int k = 0; k < R; ++k) {
+#pragma unroll
+      for (int e = 0; e < V; ++e) {
+        float acc = bv[e];
+        if (wt) {
+#pragma unroll
+          for (int j = 0; j < KS; ++j) acc += wj[j][e] * xin[k + j][e];
+        } else {
+          acc += xin[k + KS - 1][e];
+        }
+        o[k][e] = silu_(acc);
+        ss[k] += o[k][e] * o[k][e];
+      }
+    }
+  }
+  float inv[R];
+#pragma unroll
+  for (int k = 0; k < R; ++k) inv[k] = 1.f;
+  if (normalize) {
+#pragma unroll
+    for (int k = 0; k < R; ++k) {
+      const float v = warp_sum(ss[k]);
+      if (lane == 0) red[threadIdx.y][k][wir] = v;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < R; ++k) {
+      float tot = 0.f;
+      for (int w = 0; w < nw; ++w) tot += red[threadIdx.y][k][w];
+      inv[k] = 1.f / fmaxf(sqrtf(tot), kL2Eps);
+    }
+  }
+  if (active) {
+#pragma unroll
+    for (int k = 0; k < R; ++k) {
+#pragma unroll
+      for (int e = 0; e < V; ++e) o[k][e] *= inv[k];
+      store16<T>(y + (r0 + k) * D + col, o[k]);
+    }
+  }
+}
+
 // dc = d(loss)/d(conv output) (fp32, [rows, D]); without a conv it writes dx directly.
 template <typename T, int KS>
 __global__ void __launch_bounds__(512) conv_bwd_a_rows(const T* __restrict__ dy, const T* __restrict__ x,
@@ -360,11 +436,25 @@ at::Tensor conv_silu_norm_fwd(const at::Tensor& x, const c10::optional<at::Tenso
   TB_DISPATCH_BF16_F32(x.scalar_type(), "conv_silu_norm_fwd", [&] {
     constexpr int V = Vec16<scalar_t>::N;
     check_x(x, V);
-    const dim3 blk = row_block(threads_for(D, V));
-    const int64_t grid = (rows + blk.y - 1) / blk.y;
-    TB_KS_SWITCH(K, conv_fwd_rows<scalar_t, KS><<<grid, blk, 0, stream()>>>(
-        (const scalar_t*)x.data_ptr(), x.stride(0), x.stride(1), wt.defined() ? (const scalar_t*)wt.data_ptr() : nullptr,
-        bias.defined() ? (const scalar_t*)bias.data_ptr() : nullptr, (scalar_t*)y.data_ptr(), rows, Tn, D, normalize));
+    const int tpr = threads_for(D, V);
+    constexpr int R = 4;
+    if (Tn % R == 0 && tpr <= 256) {
+      const dim3 blk(tpr, std::max(1, std::min(8, 256 / tpr)));
+      const int64_t grid = (rows / R + blk.y - 1) / blk.y;
+      TB_KS_SWITCH(K, conv_fwd_rrows<scalar_t, KS, R><<<grid, blk, 0, stream()>>>(
+          (const scalar_t*)x.data_ptr(), x.stride(0), x.stride(1),
+          wt.defined() ? (const scalar_t*)wt.data_ptr() : nullptr,
+          bias.defined() ? (const scalar_t*)bias.data_ptr() : nullptr, (scalar_t*)y.data_ptr(), rows, Tn, D,
+          normalize));
+    } else {
+      const dim3 blk = row_block(tpr);
+      const int64_t grid = (rows + blk.y - 1) / blk.y;
+      TB_KS_SWITCH(K, conv_fwd_rows<scalar_t, KS><<<grid, blk, 0, stream()>>>(
+          (const scalar_t*)x.data_ptr(), x.stride(0), x.stride(1),
+          wt.defined() ? (const scalar_t*)wt.data_ptr() : nullptr,
+          bias.defined() ? (const scalar_t*)bias.data_ptr() : nullptr, (scalar_t*)y.data_ptr(), rows, Tn, D,
+          normalize));
+    }
   });
   check_launch("conv_silu_norm_fwd");
   return y;

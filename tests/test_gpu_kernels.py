@@ -205,13 +205,14 @@ TC_CASES = [
 ]
 
 
+@pytest.mark.parametrize("d", [64, 96])
 @pytest.mark.parametrize("case", TC_CASES)
-def test_attention_tcgen05_forward(case):
-    """tcgen05 forward vs the mma.sync forward and an fp32 dense-mask reference."""
+def test_attention_tcgen05_forward(case, d):
+    """tcgen05 forward (head dim 64, or 96 with split 128/64-byte-swizzled tiles)
+    vs the mma.sync forward and an fp32 dense-mask reference."""
     B, H, T, P, W = case
     E = _ext.ext()
     torch.manual_seed(7)
-    d = 64
     Q = torch.randn(B, H, T, d, device=DEV, dtype=torch.bfloat16)
     K = torch.randn(B, H, P + T, d, device=DEV, dtype=torch.bfloat16)
     V = torch.randn(B, H, P + T, d, device=DEV, dtype=torch.bfloat16)

@@ -34,20 +34,29 @@ namespace attn_tc {
 
 using bf16 = __nv_bfloat16;
 
-constexpr int HD = 64;
 constexpr int BM = 128;  // rows per query tile
 constexpr int NQ = 2;    // query tiles per CTA
 constexpr int BN = 128;  // keys per tile
 constexpr int NS = 2;    // K/V stages
-constexpr int TILE_Q = BM * HD * 2;
-constexpr int TILE_K = BN * HD * 2;
 constexpr int TILE_P = BM * BN * 2;
-constexpr int OFF_Q = 0;
-constexpr int OFF_K = OFF_Q + NQ * TILE_Q;
-constexpr int OFF_V = OFF_K + NS * TILE_K;
-constexpr int OFF_P = OFF_V + NS * TILE_K;
-constexpr int OFF_BAR = OFF_P + NQ * TILE_P;
-constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;
+
+// Shared-memory layout for head dim HD (64 or 96).  A Q/K/V tile holds
+// columns 0-63 as 128-byte rows (128-byte swizzle) and, for HD = 96, columns
+// 64-95 right after them as 64-byte rows (64-byte swizzle): 24 KB per 128 rows
+// instead of the 32 KB a padding to 128 columns would take, so two query
+// tiles, two K/V stages and two P tiles still fit (208 KB).
+template <int HD>
+struct Fwd {
+  static_assert(HD == 64 || HD == 96, "head_dim 64 or 96");
+  static constexpr int TILE_QA = BM * 64 * 2, TILE_QB = HD > 64 ? BM * 32 * 2 : 0, TILE_Q = TILE_QA + TILE_QB;
+  static constexpr int TILE_KA = BN * 64 * 2, TILE_KB = HD > 64 ? BN * 32 * 2 : 0, TILE_K = TILE_KA + TILE_KB;
+  static constexpr int OFF_Q = 0;
+  static constexpr int OFF_K = OFF_Q + NQ * TILE_Q;
+  static constexpr int OFF_V = OFF_K + NS * TILE_K;
+  static constexpr int OFF_P = OFF_V + NS * TILE_K;
+  static constexpr int OFF_BAR = OFF_P + NQ * TILE_P;
+  static constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;
+};
 constexpr uint32_t TM_S = 0, TM_O = 256, TM_COLS = 512;
 constexpr int NTHREADS = 320;
 
@@ -119,13 +128,20 @@ __device__ __forceinline__ void exp2_poly2(float x0, float x1, float& y0, float&
   y1 = x1 < -125.f ? 0.f : __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23));
 }
 
+// tmQ/tmK/tmV: columns 0-63 (128-byte swizzle); tmQb/tmKb/tmVb: columns 64-95
+// (64-byte swizzle), used when HD = 96.
+template <int HD>
 __global__ void __launch_bounds__(NTHREADS, 1)
     attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                       const __grid_constant__ CUtensorMap tmV, bf16* __restrict__ O, float* __restrict__ LSE,
+                       const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmQb,
+                       const __grid_constant__ CUtensorMap tmKb, const __grid_constant__ CUtensorMap tmVb,
+                       bf16* __restrict__ O, float* __restrict__ LSE,
                        int H, int Tn, int P, int W, float scale_log2, unsigned* __restrict__ err) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
+  using C = Fwd<HD>;
+  constexpr bool kSplit = HD > 64;  // columns 64-95 in a second, 64-byte-swizzled tile
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
   uint64_t* bar_q = bars + 0;
   uint64_t* bar_kv_full = bars + 1;          // [NS]
   uint64_t* bar_kv_empty = bars + 1 + NS;    // [NS]
@@ -178,16 +194,24 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       tc::tma_prefetch_desc(&tmQ);
       tc::tma_prefetch_desc(&tmK);
       tc::tma_prefetch_desc(&tmV);
-      tc::mbar_expect_tx(bar_q, NQ * TILE_Q);
-      for (int q = 0; q < NQ; ++q) tc::tma_load_3d(smem + OFF_Q + q * TILE_Q, &tmQ, bar_q, 0, m0 + q * BM, bh);
+      tc::mbar_expect_tx(bar_q, NQ * C::TILE_Q);
+      for (int q = 0; q < NQ; ++q) {
+        tc::tma_load_3d(smem + C::OFF_Q + q * C::TILE_Q, &tmQ, bar_q, 0, m0 + q * BM, bh);
+        if constexpr (kSplit)
+          tc::tma_load_3d(smem + C::OFF_Q + q * C::TILE_Q + C::TILE_QA, &tmQb, bar_q, 64, m0 + q * BM, bh);
+      }
       int issued = 0;
       for (int it = 0; it < n_tiles; ++it) {
         const int s = it % NS;
         if (it >= NS && !tc::mbar_wait(bar_kv_empty + s, ((it / NS) - 1) & 1, abort_flag, err)) break;
         const int n0 = tile_n0(it);
-        tc::mbar_expect_tx(bar_kv_full + s, 2 * TILE_K);
-        tc::tma_load_3d(smem + OFF_K + s * TILE_K, &tmK, bar_kv_full + s, 0, n0, bh);
-        tc::tma_load_3d(smem + OFF_V + s * TILE_K, &tmV, bar_kv_full + s, 0, n0, bh);
+        tc::mbar_expect_tx(bar_kv_full + s, 2 * C::TILE_K);
+        tc::tma_load_3d(smem + C::OFF_K + s * C::TILE_K, &tmK, bar_kv_full + s, 0, n0, bh);
+        tc::tma_load_3d(smem + C::OFF_V + s * C::TILE_K, &tmV, bar_kv_full + s, 0, n0, bh);
+        if constexpr (kSplit) {
+          tc::tma_load_3d(smem + C::OFF_K + s * C::TILE_K + C::TILE_KA, &tmKb, bar_kv_full + s, 64, n0, bh);
+          tc::tma_load_3d(smem + C::OFF_V + s * C::TILE_K + C::TILE_KA, &tmVb, bar_kv_full + s, 64, n0, bh);
+        }
         issued = it + 1;
       }
       if (*abort_flag) {
@@ -200,15 +224,22 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0 && n_tiles > 0) {
       constexpr uint32_t idesc_s = tc::idesc_bf16_f32(BM, BN, false, false);
-      constexpr uint32_t idesc_o = tc::idesc_bf16_f32(BM, HD, false, true);
+      constexpr uint32_t idesc_o = tc::idesc_bf16_f32(BM, 64, false, true);    // O columns 0-63
+      constexpr uint32_t idesc_o2 = tc::idesc_bf16_f32(BM, 32, false, true);   // O columns 64-95 (HD = 96)
       bool ok = tc::mbar_wait(bar_q, 0, abort_flag, err);
       auto issue_s = [&](int q, int it) {
-        const uint32_t aQ = tc::smem_addr(smem + OFF_Q + q * TILE_Q);
-        const uint32_t aK = tc::smem_addr(smem + OFF_K + (it % NS) * TILE_K);
+        const uint32_t aQ = tc::smem_addr(smem + C::OFF_Q + q * C::TILE_Q);
+        const uint32_t aK = tc::smem_addr(smem + C::OFF_K + (it % NS) * C::TILE_K);
 #pragma unroll
-        for (int k = 0; k < HD / 16; ++k)
+        for (int k = 0; k < 4; ++k)
           tc::umma_bf16(tmem + TM_S + q * BN, tc::sdesc_sw128(aQ + 32 * k, 16, 1024),
                         tc::sdesc_sw128(aK + 32 * k, 16, 1024), idesc_s, k > 0);
+        if constexpr (kSplit) {
+#pragma unroll
+          for (int k = 0; k < 2; ++k)
+            tc::umma_bf16(tmem + TM_S + q * BN, tc::sdesc_sw64(aQ + C::TILE_QA + 32 * k, 16, 512),
+                          tc::sdesc_sw64(aK + C::TILE_KA + 32 * k, 16, 512), idesc_s, 1u);
+        }
         tc::umma_commit(bar_s_full + q);
       };
       if (ok) ok = tc::mbar_wait(bar_kv_full, 0, abort_flag, err);
@@ -220,19 +251,23 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       for (int it = 0; ok && it < n_tiles; ++it) {
         const int s = it % NS;
         const bool more = it + 1 < n_tiles;
-        const uint32_t aV = tc::smem_addr(smem + OFF_V + s * TILE_K);
+        const uint32_t aV = tc::smem_addr(smem + C::OFF_V + s * C::TILE_K);
         for (int q = 0; q < NQ && ok; ++q) {
           if (!tc::mbar_wait(bar_p_full + q, it & 1, abort_flag, err)) {
             ok = false;
             break;
           }
           tc::tc_fence_after();
-          const uint32_t aP = tc::smem_addr(smem + OFF_P + q * TILE_P);
+          const uint32_t aP = tc::smem_addr(smem + C::OFF_P + q * TILE_P);
 #pragma unroll
           for (int k = 0; k < BN / 16; ++k) {
             const uint64_t ad = tc::sdesc_sw128(aP + (k >> 2) * (BM * 128) + (k & 3) * 32, 16, 1024);
             const uint64_t bd = tc::sdesc_sw128(aV + k * 2048, BN * 128, 1024);  // V: MN-major
             tc::umma_bf16(tmem + TM_O + q * HD, ad, bd, idesc_o, (it > 0 || k > 0) ? 1u : 0u);
+            if constexpr (kSplit) {
+              const uint64_t bd2 = tc::sdesc_sw64(aV + C::TILE_KA + k * 1024, BN * 64, 512);
+              tc::umma_bf16(tmem + TM_O + q * HD + 64, ad, bd2, idesc_o2, (it > 0 || k > 0) ? 1u : 0u);
+            }
           }
           tc::umma_commit(bar_o_done + q);
           if (q == NQ - 1) tc::umma_commit(bar_kv_empty + s);
@@ -256,7 +291,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     const int i = m0 + q * BM + row;      // query index
     const uint32_t tl = tmem + ((uint32_t)((warp & 3) * 32) << 16);
     const uint32_t tS = tl + TM_S + q * BN, tO = tl + TM_O + q * HD;
-    uint8_t* sP = smem + OFF_P + q * TILE_P;
+    uint8_t* sP = smem + C::OFF_P + q * TILE_P;
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
     const int win_lo = max(0, i - W + 1), win_hi = min(i, Tn - 1);  // visible main keys [win_lo, win_hi]
@@ -445,17 +480,25 @@ EncodeTiledFn encode_tiled_fn() {
   return fn;
 }
 
-CUtensorMap make_map_3d(const void* base, uint64_t inner, uint64_t rows, uint64_t outer, uint32_t box_rows) {
+// box_cols 64: 128-byte rows with the 128-byte swizzle; 32: 64-byte rows with the 64-byte swizzle
+CUtensorMap make_map_3d(const void* base, uint64_t inner, uint64_t rows, uint64_t outer, uint32_t box_rows,
+                        uint32_t box_cols) {
+  TORCH_CHECK(box_cols == 64 || box_cols == 32, "make_map_3d: box of 64 or 32 columns");
   CUtensorMap m;
   cuuint64_t dims[3] = {inner, rows, outer};
   cuuint64_t strides[2] = {inner * 2, inner * rows * 2};
-  cuuint32_t box[3] = {64, box_rows, 1};
+  cuuint32_t box[3] = {box_cols, box_rows, 1};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = encode_tiled_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides,
-                                      box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                      box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                      box_cols == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
                                       CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed: ", (int)r);
   return m;
+}
+
+CUtensorMap make_map_3d(const void* base, uint64_t inner, uint64_t rows, uint64_t outer, uint32_t box_rows) {
+  return make_map_3d(base, inner, rows, outer, box_rows, 64);
 }
 
 }  // namespace attn_tc
@@ -475,7 +518,8 @@ int64_t kernel_error_status(int64_t device, bool reset) {
   return v;
 }
 
-bool attn_tc_supported(int64_t head_dim) { return head_dim == attn_tc::HD; }
+bool attn_tc_supported(int64_t head_dim) { return head_dim == 64; }             // backward
+bool attn_tc_fwd_supported(int64_t head_dim) { return head_dim == 64 || head_dim == 96; }
 
 // Same contract as attn_fwd_packed: Q [B,H,T,64], K/V [B,H,P+T,64] bf16 contiguous
 // -> {O [B,T,H,64] bf16, LSE [B,H,T] fp32}
@@ -485,7 +529,7 @@ std::vector<at::Tensor> attn_fwd_tc(const at::Tensor& Q, const at::Tensor& K, co
   TORCH_CHECK(Q.scalar_type() == at::kBFloat16 && Q.is_contiguous() && K.is_contiguous() && V.is_contiguous(),
               "attn_fwd_tc: packed bf16 inputs");
   const int B = Q.size(0), H = Q.size(1), Tn = Q.size(2), hd = Q.size(3);
-  TORCH_CHECK(hd == attn_tc::HD, "attn_fwd_tc: head_dim must be 64");
+  TORCH_CHECK(hd == 64 || hd == 96, "attn_fwd_tc: head_dim must be 64 or 96");
   const int L = K.size(2), P = L - Tn;
   TORCH_CHECK(aligned16(Q) && aligned16(K) && aligned16(V), "attn_fwd_tc: 16-byte aligned inputs required");
   at::Tensor O = at::empty({B, Tn, H, hd}, Q.options());
@@ -494,17 +538,33 @@ std::vector<at::Tensor> attn_fwd_tc(const at::Tensor& Q, const at::Tensor& K, co
   const CUtensorMap mq = attn_tc::make_map_3d(Q.data_ptr(), hd, Tn, (uint64_t)B * H, attn_tc::BM);
   const CUtensorMap mk = attn_tc::make_map_3d(K.data_ptr(), hd, L, (uint64_t)B * H, attn_tc::BN);
   const CUtensorMap mv = attn_tc::make_map_3d(V.data_ptr(), hd, L, (uint64_t)B * H, attn_tc::BN);
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaFuncSetAttribute(attn_tc::attn_fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         attn_tc::SMEM_BYTES);
-    attr_set = true;
-  }
   const int W = (int)std::min<int64_t>(window, 1 << 30);
   dim3 grid((Tn + attn_tc::NQ * attn_tc::BM - 1) / (attn_tc::NQ * attn_tc::BM), B * H);
-  attn_tc::attn_fwd_tc_kernel<<<grid, attn_tc::NTHREADS, attn_tc::SMEM_BYTES, stream()>>>(
-      mq, mk, mv, (__nv_bfloat16*)O.data_ptr(), LSE.data_ptr<float>(), H, Tn, P, W,
-      (float)scale * 1.4426950408889634f, (unsigned*)tc_error_word(Q.device()).data_ptr<int>());
+  const float sl2 = (float)scale * 1.4426950408889634f;
+  unsigned* err = (unsigned*)tc_error_word(Q.device()).data_ptr<int>();
+  if (hd == 64) {
+    static bool attr_set = false;
+    if (!attr_set) {
+      C10_CUDA_CHECK(cudaFuncSetAttribute(attn_tc::attn_fwd_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          attn_tc::Fwd<64>::SMEM_BYTES));
+      attr_set = true;
+    }
+    attn_tc::attn_fwd_tc_kernel<64><<<grid, attn_tc::NTHREADS, attn_tc::Fwd<64>::SMEM_BYTES, stream()>>>(
+        mq, mk, mv, mq, mk, mv, (__nv_bfloat16*)O.data_ptr(), LSE.data_ptr<float>(), H, Tn, P, W, sl2, err);
+  } else {
+    // columns 64-95: 32-column boxes with the 64-byte swizzle, loaded at x = 64
+    const CUtensorMap mq2 = attn_tc::make_map_3d(Q.data_ptr(), hd, Tn, (uint64_t)B * H, attn_tc::BM, 32);
+    const CUtensorMap mk2 = attn_tc::make_map_3d(K.data_ptr(), hd, L, (uint64_t)B * H, attn_tc::BN, 32);
+    const CUtensorMap mv2 = attn_tc::make_map_3d(V.data_ptr(), hd, L, (uint64_t)B * H, attn_tc::BN, 32);
+    static bool attr_set = false;
+    if (!attr_set) {
+      C10_CUDA_CHECK(cudaFuncSetAttribute(attn_tc::attn_fwd_tc_kernel<96>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          attn_tc::Fwd<96>::SMEM_BYTES));
+      attr_set = true;
+    }
+    attn_tc::attn_fwd_tc_kernel<96><<<grid, attn_tc::NTHREADS, attn_tc::Fwd<96>::SMEM_BYTES, stream()>>>(
+        mq, mk, mv, mq2, mk2, mv2, (__nv_bfloat16*)O.data_ptr(), LSE.data_ptr<float>(), H, Tn, P, W, sl2, err);
+  }
   check_launch("attn_fwd_tc");
   return {O, LSE};
 }

@@ -51,6 +51,7 @@ std::vector<at::Tensor> attn_unpack(const at::Tensor& dQa, const at::Tensor& dKa
 // attention_tc.cu
 std::vector<at::Tensor> attn_fwd_tc(const at::Tensor& Q, const at::Tensor& K, const at::Tensor& V, int64_t window,
                                     double scale);
+bool attn_tc_fwd_supported(int64_t head_dim);
 bool attn_tc_supported(int64_t head_dim);
 std::vector<at::Tensor> attn_bwd_tc(const at::Tensor& dO, const at::Tensor& Q, const at::Tensor& K,
                                     const at::Tensor& V, const at::Tensor& O, const at::Tensor& LSE, int64_t window,
@@ -111,6 +112,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_unpack", &tb::attn_unpack);
   m.def("attn_fwd_tc", &tb::attn_fwd_tc);
   m.def("attn_tc_supported", &tb::attn_tc_supported);
+  m.def("attn_tc_fwd_supported", &tb::attn_tc_fwd_supported);
   m.def("attn_bwd_tc", &tb::attn_bwd_tc);
   m.def("memory_scan_fwd", &tb::memory_scan_fwd);
   m.def("comm_alloc", &tb::comm_alloc);

@@ -142,6 +142,18 @@ __device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr, uint32_t lbo_byt
   return d;
 }
 
+// Same with the 64-byte swizzle (layout type 4): rows of 64 bytes, 8-row
+// atoms of 512 bytes.
+__device__ __forceinline__ uint64_t sdesc_sw64(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)4 << 61;
+  return d;
+}
+
 // Instruction descriptor for kind::f16 with bf16 A/B and fp32 accumulation.
 __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N, bool a_mn_major, bool b_mn_major) {
   return (1u << 4)     // C format: F32

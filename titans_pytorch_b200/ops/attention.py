@@ -94,10 +94,10 @@ class _WindowAttnFn(torch.autograd.Function):
     def forward(ctx, qkv, pkv, H, window, scale, inv_freq):
         E = ext()
         Q, K, V = E.attn_pack(qkv, pkv, H, inv_freq)
-        if E.attn_tc_supported(Q.shape[-1]):
-            O, lse = E.attn_fwd_tc(Q, K, V, window, scale)      # tcgen05 / TMEM / TMA
+        if E.attn_tc_fwd_supported(Q.shape[-1]):
+            O, lse = E.attn_fwd_tc(Q, K, V, window, scale)      # tcgen05 / TMEM / TMA (head_dim 64, 96)
         else:
-            O, lse = E.attn_fwd_packed(Q, K, V, window, scale)  # mma.sync path (head_dim != 64)
+            O, lse = E.attn_fwd_packed(Q, K, V, window, scale)  # mma.sync path (other head dims)
         ctx.save_for_backward(Q, K, V, O, lse, inv_freq)
         ctx.window, ctx.scale = window, scale
         ctx.bp = 0 if pkv is None else pkv.shape[0]

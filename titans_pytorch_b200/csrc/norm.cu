@@ -193,7 +193,7 @@ std::vector<at::Tensor> rms_norm_bwd(const at::Tensor& dy, const at::Tensor& x, 
     if (need_dw) dw.zero_();
     return {dx, dw};
   }
-  const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>((rows + 7) / 8, (int64_t)num_sms() * 2));
+  const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>((rows + 7) / 8, (int64_t)num_sms() * 3));
   at::Tensor part = need_dw ? at::empty({blocks, D}, x.options().dtype(at::kFloat)) : at::Tensor();
   TB_DISPATCH_FLOAT(x.scalar_type(), "rms_norm_bwd", [&] {
     constexpr int V = Vec16<scalar_t>::N;

@@ -278,3 +278,21 @@ def test_fused_add_rms_norm_kernel(dtype, D):
     torch.testing.assert_close(x.grad.float(), xf.grad, **tol)
     torch.testing.assert_close(r.grad.float(), rf.grad, **tol)
     torch.testing.assert_close(w.grad.float(), wf.grad, atol=0.5 if dtype == torch.bfloat16 else 1e-2, rtol=2e-2)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("shape", [(3, 40, 256), (7, 3072)])
+def test_silu_activation_kernel(dtype, shape):
+    """Memory-MLP SiLU on the extension's kernels vs F.silu in fp32 (value and gradient)."""
+    from titans_pytorch_b200.ops.memory import activation
+
+    torch.manual_seed(5)
+    z = torch.randn(*shape, device=DEV, dtype=dtype, requires_grad=True)
+    a = activation(z, "silu")
+    zr = z.detach().float().requires_grad_()
+    ar = F.silu(zr)
+    assert rel_err(a, ar) < 1e-2
+    g = torch.randn_like(ar)
+    a.backward(g.to(dtype))
+    ar.backward(g)
+    assert rel_err(z.grad, zr.grad) < 1e-2

@@ -22,6 +22,7 @@ at::Tensor memory_gates(const at::Tensor& x, const std::vector<at::Tensor>& ws, 
                         double lr, double mom);
 void act_inplace(const at::Tensor& z, at::Tensor& a, const std::string& act);
 void act_grad_mul(at::Tensor& gr, const at::Tensor& z, const std::string& act);
+void act_grad_out(const at::Tensor& g, const at::Tensor& z, at::Tensor& out, const std::string& act);
 void scaled_err(at::Tensor& p, const at::Tensor& v, double scale);
 std::vector<at::Tensor> mem_update(const at::Tensor& w, const at::Tensor& m, const at::Tensor& grad,
                                    const at::Tensor& gates);
@@ -95,6 +96,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("memory_gates", &tb::memory_gates);
   m.def("act_inplace", &tb::act_inplace);
   m.def("act_grad_mul", &tb::act_grad_mul);
+  m.def("act_grad_out", &tb::act_grad_out);
   m.def("scaled_err", &tb::scaled_err);
   m.def("mem_update", &tb::mem_update);
   m.def("cross_entropy_fwd", &tb::cross_entropy_fwd);

@@ -112,6 +112,21 @@ __global__ void act_grad_mul_kernel(T* __restrict__ g, const T* __restrict__ z, 
   }
 }
 
+// out <- g * act'(z)  (out of place: the autograd backward of an activation)
+template <typename T>
+__global__ void act_grad_out_kernel(const T* __restrict__ g, const T* __restrict__ z, T* __restrict__ out,
+                                    int64_t nvec, int act) {
+  constexpr int V = Vec16<T>::N;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nvec; i += (int64_t)gridDim.x * blockDim.x) {
+    float gv[V], zv[V];
+    load16<T>(g + i * V, gv);
+    load16<T>(z + i * V, zv);
+#pragma unroll
+    for (int k = 0; k < V; ++k) gv[k] *= act_grad_f(act, zv[k]);
+    store16<T>(out + i * V, gv);
+  }
+}
+
 // d <- (p - v) * scale   (in place on p)
 template <typename T>
 __global__ void scaled_err_kernel(T* __restrict__ p, const T* __restrict__ v, int64_t nvec, float scale) {
@@ -299,6 +314,23 @@ void act_grad_mul(at::Tensor& gr, const at::Tensor& z, const std::string& act) {
     if (n) act_grad_mul_kernel<scalar_t><<<ew_blocks(n), 256, 0, stream()>>>((scalar_t*)gr.data_ptr(), (const scalar_t*)z.data_ptr(), n, act_code(act));
   });
   check_launch("act_grad_mul");
+}
+
+void act_grad_out(const at::Tensor& g, const at::Tensor& z, at::Tensor& out, const std::string& act) {
+  const at::cuda::CUDAGuard guard(z.device());
+  TORCH_CHECK(z.is_contiguous() && g.is_contiguous() && out.is_contiguous() && aligned16(z) && aligned16(g) &&
+                  aligned16(out) && g.numel() == z.numel() && out.numel() == z.numel() &&
+                  g.scalar_type() == z.scalar_type() && out.scalar_type() == z.scalar_type(),
+              "act_grad_out: contiguous aligned tensors of one shape and dtype required");
+  TB_DISPATCH_FLOAT(z.scalar_type(), "act_grad_out", [&] {
+    constexpr int V = Vec16<scalar_t>::N;
+    TORCH_CHECK(z.numel() % V == 0, "act_grad_out: numel must be a multiple of ", V);
+    const int64_t n = z.numel() / V;
+    if (n)
+      act_grad_out_kernel<scalar_t><<<ew_blocks(n), 256, 0, stream()>>>(
+          (const scalar_t*)g.data_ptr(), (const scalar_t*)z.data_ptr(), (scalar_t*)out.data_ptr(), n, act_code(act));
+  });
+  check_launch("act_grad_out");
 }
 
 void scaled_err(at::Tensor& p, const at::Tensor& v, double scale) {

@@ -32,7 +32,7 @@ import torch.nn.functional as F
 
 from ..config import TitansConfig
 from ..ops.conv import conv_silu_norm
-from ..ops.memory import (activation_fn, memory_grads_reference, memory_step,
+from ..ops.memory import (activation, activation_fn, memory_grads_reference, memory_step,
                           mlp_forward_reference)
 from ..ops.linear import linear
 from ..ops.memory_paper import head_blocks, memory_scan, memory_scan_reference
@@ -86,12 +86,12 @@ class MemoryMLP(nn.Module):
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         # same math as mlp_forward_reference; the weight gradients go through
         # ops.linear (accumulated in place under the trainer)
-        f = activation_fn(self.config.activation)
+        act, uk = self.config.activation, getattr(self.config, "use_kernels", None)
         h = x
         for i, layer in enumerate(self.layers):
             h = linear(h, layer.weight)
             if i < self.num_layers - 1:
-                h = f(h)
+                h = activation(h, act, uk)
         return h
 
     def get_weights(self) -> list[torch.Tensor]:

@@ -44,6 +44,35 @@ def activation_fn(name: str):
     raise ValueError(f"Unknown activation: {name}")
 
 
+class _SiLU(torch.autograd.Function):
+    """silu(z) on the extension's vectorised kernels: the forward keeps z, the
+    backward writes g * silu'(z) to a new tensor (one read of g and z, one write)."""
+
+    @staticmethod
+    def forward(ctx, z):
+        a = torch.empty_like(z)
+        ext().act_inplace(z, a, "silu")
+        ctx.save_for_backward(z)
+        return a
+
+    @staticmethod
+    def backward(ctx, g):
+        (z,) = ctx.saved_tensors
+        g = g.contiguous()
+        out = torch.empty_like(z)
+        ext().act_grad_out(g, z, out, "silu")
+        return out
+
+
+def activation(z: torch.Tensor, name: str, use_kernels: bool | None = None) -> torch.Tensor:
+    """``act(z)``; SiLU on CUDA (bf16 / fp32, contiguous, 16-byte aligned) runs the
+    extension's kernels, everything else ``activation_fn(name)``."""
+    if (name == "silu" and want_kernels(z, use_kernels) and z.dtype in (torch.bfloat16, torch.float32)
+            and z.is_contiguous() and z.numel() % (16 // z.element_size()) == 0 and z.data_ptr() % 16 == 0):
+        return _SiLU.apply(z)
+    return activation_fn(name)(z)
+
+
 def activation_grad(name: str, z: torch.Tensor) -> torch.Tensor:
     """d act(z) / dz, elementwise."""
     if name == "silu":

@@ -81,6 +81,11 @@ at::Tensor gemm_tc(const at::Tensor& A, const at::Tensor& B);
 at::Tensor gemm_gather_tc(const at::Tensor& A, const at::Tensor& B, at::Tensor& flat, const at::Tensor& src_ptrs,
                           int64_t u0, int64_t len, int64_t shard, int64_t me, bool consume);
 void fsdp_gather(at::Tensor& flat, const at::Tensor& src_ptrs, int64_t u0, int64_t len, int64_t shard, int64_t me);
+// gemm_sm100.cu
+void gemm_sm100(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn, int64_t M, int64_t N, int64_t K,
+                int64_t mode, const at::Tensor& Cout, const c10::optional<at::Tensor>& R,
+                const c10::optional<at::Tensor>& C2, const c10::optional<at::Tensor>& R2,
+                const c10::optional<at::Tensor>& gates, double scale, int64_t act, int64_t ffn_f, int64_t splits);
 }  // namespace tb
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -133,5 +138,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_tc", &tb::gemm_tc);
   m.def("gemm_gather_tc", &tb::gemm_gather_tc);
   m.def("fsdp_gather", &tb::fsdp_gather);
+  m.def("gemm_sm100", &tb::gemm_sm100, pybind11::arg("A"), pybind11::arg("a_mn"), pybind11::arg("B"),
+        pybind11::arg("b_mn"), pybind11::arg("M"), pybind11::arg("N"), pybind11::arg("K"), pybind11::arg("mode"),
+        pybind11::arg("C"), pybind11::arg("R") = pybind11::none(), pybind11::arg("C2") = pybind11::none(),
+        pybind11::arg("R2") = pybind11::none(), pybind11::arg("gates") = pybind11::none(),
+        pybind11::arg("scale") = 1.0, pybind11::arg("act") = 0, pybind11::arg("ffn_f") = 0,
+        pybind11::arg("splits") = 0);
   m.def("kernel_error_status", &tb::kernel_error_status, pybind11::arg("device") = 0, pybind11::arg("reset") = true);
 }

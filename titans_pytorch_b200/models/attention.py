@@ -79,23 +79,9 @@ class _AttentionBase(nn.Module):
         for m in (self.proj_q, self.proj_k, self.proj_v, self.proj_out):
             nn.init.normal_(m.weight, std=config.init_std)
 
-    # Set by the owning model: a per-forward cache of derived weights, so a MAC
-    # forward without autograd (inference) concatenates q|k|v once instead of
-    # once per segment.  With autograd the concatenation is rebuilt per use:
-    # sharing it would sum the segments' gradients out of place at the shared
-    # node instead of accumulating them in place into each weight's .grad.
+    # Set by the owning model (a per-forward cache of derived weights); the
+    # stacked projections below read adjacent weights in place, so nothing is cached.
     _wcache: dict | None = None
-
-    def _qkv_weight(self) -> torch.Tensor:
-        key = (id(self), "qkv")
-        use = self._wcache is not None and self._wcache.get("active") and not torch.is_grad_enabled()
-        cache = self._wcache if use else None
-        if cache is not None and key in cache:
-            return cache[key]
-        w = torch.cat([self.proj_q.weight, self.proj_k.weight, self.proj_v.weight], dim=0)
-        if cache is not None:
-            cache[key] = w
-        return w
 
     def _attend(self, qkv, pkv, window):
         """qkv: [B, T, 3D]; pkv: [B or 1, P, 2D] or None -> [B, T, D] after proj_out."""
@@ -103,17 +89,14 @@ class _AttentionBase(nn.Module):
             qkv, pkv, self.num_heads, window=window, scale=self.scale,
             inv_freq=None if self.rope is None else self.rope.inv_freq,
             dropout_p=self.dropout.p, training=self.training, use_kernels=self.use_kernels)
-        return linear(o.reshape(*qkv.shape[:-1], self.dim), self.proj_out.weight)
+        return linear(o.reshape(*qkv.shape[:-1], self.dim), self.proj_out.weight, use_kernels=self.use_kernels)
 
     def _project(self, x: torch.Tensor, kv_only: bool = False) -> torch.Tensor:
         """x @ [Wq; Wk; Wv]^T (or [Wk; Wv] with ``kv_only``); weight gradients
         accumulate in place under the trainer (see ``ops.linear``)."""
-        if not torch.is_grad_enabled():
-            w = self._qkv_weight()
-            return F.linear(x, w[self.dim:] if kv_only else w)
         ws = (self.proj_k.weight, self.proj_v.weight) if kv_only else (
             self.proj_q.weight, self.proj_k.weight, self.proj_v.weight)
-        return linear(x, *ws)
+        return linear(x, *ws, use_kernels=self.use_kernels)
 
 
 class SlidingWindowAttention(_AttentionBase):

@@ -44,6 +44,8 @@ class FeedForward(nn.Module):
         self.down_proj = nn.Linear(config.ffn_dim, config.dim, bias=False)
         self.dropout = nn.Dropout(config.dropout)
 
-    def forward(self, x: torch.Tensor) -> torch.Tensor:
+    def forward(self, x: torch.Tensor, residual: torch.Tensor | None = None) -> torch.Tensor:
+        """``ffn(x)``, or ``residual + ffn(x)`` with the add fused into the down projection
+        (the caller's dropout on the FFN output must be inactive to pass ``residual``)."""
         return swiglu_ffn(x, self.gate_proj.weight, self.up_proj.weight, self.down_proj.weight,
-                          self.dropout.p, self.training, self.use_kernels)
+                          self.dropout.p, self.training, self.use_kernels, residual=residual)

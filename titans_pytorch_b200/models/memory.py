@@ -32,8 +32,8 @@ import torch.nn.functional as F
 
 from ..config import TitansConfig
 from ..ops.conv import conv_silu_norm
-from ..ops.memory import (activation, activation_fn, memory_grads_reference, memory_step,
-                          mlp_forward_reference)
+from ..ops.memory import (activation, activation_fn, memory_grads_reference, memory_mlp, memory_step,
+                          mlp_forward_reference, mlp_kernel_ok)
 from ..ops.linear import linear
 from ..ops.memory_paper import head_blocks, memory_scan, memory_scan_reference
 
@@ -84,12 +84,16 @@ class MemoryMLP(nn.Module):
         return [layer.weight for layer in self.layers]
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        # same math as mlp_forward_reference; the weight gradients go through
-        # ops.linear (accumulated in place under the trainer)
+        # same math as mlp_forward_reference; on CUDA (bf16) one fused tcgen05
+        # autograd node, else ops.linear per layer (weight gradients accumulated
+        # in place under the trainer either way)
         act, uk = self.config.activation, getattr(self.config, "use_kernels", None)
+        ws = self.weight_list()
+        if mlp_kernel_ok(x, ws, act, uk):
+            return memory_mlp(x, ws, act)
         h = x
         for i, layer in enumerate(self.layers):
-            h = linear(h, layer.weight)
+            h = linear(h, layer.weight, use_kernels=uk)
             if i < self.num_layers - 1:
                 h = activation(h, act, uk)
         return h
@@ -173,25 +177,16 @@ class NeuralLongTermMemory(nn.Module):
 
     def _queries(self, x: torch.Tensor) -> torch.Tensor:
         wq, bq = self._conv("conv_q")
-        return conv_silu_norm(linear(x, self.proj_q.weight), wq, bq, True, self.use_kernels)
+        return conv_silu_norm(linear(x, self.proj_q.weight, use_kernels=self.use_kernels), wq, bq, True,
+                              self.use_kernels)
 
     # per-forward cache of derived weights, set by the owning model (see SegmentedAttention)
     _wcache: dict | None = None
 
-    def _kv_weight(self) -> torch.Tensor:
-        key = (id(self), "kv", torch.is_grad_enabled())
-        cache = self._wcache if self._wcache is not None and self._wcache.get("active") else None
-        if cache is not None and key in cache:
-            return cache[key]
-        w = torch.cat([self.proj_k.weight, self.proj_v.weight], dim=0)
-        if cache is not None:
-            cache[key] = w
-        return w
-
     @torch.no_grad()
     def _keys_values(self, x: torch.Tensor):
         D = self.dim
-        kv = F.linear(x, self._kv_weight())
+        kv = linear(x, self.proj_k.weight, self.proj_v.weight, use_kernels=self.use_kernels)
         wk, bk = self._conv("conv_k")
         wv, bv = self._conv("conv_v")
         k = conv_silu_norm(kv[..., :D], wk, bk, True, self.use_kernels)
@@ -253,10 +248,11 @@ class NeuralLongTermMemory(nn.Module):
         h, dh = self._heads()
         B, T, _ = x.shape
         wq, bq = self._conv("conv_q")
-        q = conv_silu_norm(F.linear(x, self.proj_q.weight), wq, bq, False, self.use_kernels)
+        q = conv_silu_norm(linear(x, self.proj_q.weight, use_kernels=self.use_kernels), wq, bq, False,
+                           self.use_kernels)
         q = F.normalize(self._split_heads(q), dim=-1)
         with torch.no_grad():
-            kv = F.linear(x, self._kv_weight())
+            kv = linear(x, self.proj_k.weight, self.proj_v.weight, use_kernels=self.use_kernels)
             wk, bk = self._conv("conv_k")
             wv, bv = self._conv("conv_v")
             k = F.normalize(self._split_heads(conv_silu_norm(kv[..., :D], wk, bk, False, self.use_kernels)), dim=-1)
@@ -342,7 +338,7 @@ class NeuralLongTermMemory(nn.Module):
             return (out, new_state) if return_state else (out, None)
         retrieved = self.memory(self._queries(x))
         new_state = self._update(x, state) if update else None
-        out = linear(retrieved, self.proj_out.weight)
+        out = linear(retrieved, self.proj_out.weight, use_kernels=self.use_kernels)
         return (out, new_state) if return_state else (out, None)
 
     def retrieve(self, queries: torch.Tensor, state: MemoryState) -> torch.Tensor:
@@ -350,7 +346,7 @@ class NeuralLongTermMemory(nn.Module):
         if self.paper:
             return F.linear(self._paper_retrieve(queries, state), self.proj_out.weight)
         self.memory.set_weights(state.weights)
-        return linear(self.memory(self._queries(queries)), self.proj_out.weight)
+        return linear(self.memory(self._queries(queries)), self.proj_out.weight, use_kernels=self.use_kernels)
 
 
 __all__ = ["MemoryState", "MemoryMLP", "NeuralLongTermMemory", "get_activation", "activation_fn"]

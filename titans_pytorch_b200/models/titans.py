@@ -34,6 +34,13 @@ def _norm(config: TitansConfig) -> RMSNorm:
     return RMSNorm(config.dim, config.norm_eps, config.use_kernels)
 
 
+def _ffn_residual(block: nn.Module, x: torch.Tensor, h: torch.Tensor) -> torch.Tensor:
+    """``x + dropout(ffn(h))``; the add runs in the FFN's last GEMM when dropout is off."""
+    if block.dropout.p == 0.0 or not block.training:
+        return block.ffn(h, residual=x)
+    return x + block.dropout(block.ffn(h))
+
+
 class MACBlock(nn.Module):
     def __init__(self, config: TitansConfig) -> None:
         super().__init__()
@@ -58,8 +65,7 @@ class MACBlock(nn.Module):
         # output; only the updated state is used, so only the update runs.
         new_state = self.memory._update(y, state)
         out = y * self.memory.retrieve(y, new_state)
-        out = out + self.dropout(self.ffn(self.norm2(out)))
-        return out, new_state
+        return _ffn_residual(self, out, self.norm2(out)), new_state
 
 
 class MAGBlock(nn.Module):
@@ -83,8 +89,7 @@ class MAGBlock(nn.Module):
         y = x + self.dropout(self.attention(n, prefix=self.persistent(x.shape[0])))
         m, new_state = self.memory(n, state=state, update=update_memory)
         out = y * m
-        out = out + self.dropout(self.ffn(self.norm2(out)))
-        return out, new_state
+        return _ffn_residual(self, out, self.norm2(out)), new_state
 
 
 class MALBlock(nn.Module):
@@ -107,8 +112,7 @@ class MALBlock(nn.Module):
         m, new_state = self.memory(self.norm1(x), state=state, update=update_memory)
         x, n2 = self.norm2.forward_with_residual(x, self.dropout(m))  # residual add fused with the norm
         x, n3 = self.norm3.forward_with_residual(x, self.dropout(self.attention(n2, prefix=self.persistent(x.shape[0]))))
-        x = x + self.dropout(self.ffn(n3))
-        return x, new_state
+        return _ffn_residual(self, x, n3), new_state
 
 
 class LMMBlock(nn.Module):
@@ -127,8 +131,7 @@ class LMMBlock(nn.Module):
     def forward(self, x: torch.Tensor, state: MemoryState | None = None, update_memory: bool = True):
         m, new_state = self.memory(self.norm1(x), state=state, update=update_memory)
         x, n2 = self.norm2.forward_with_residual(x, self.dropout(m))  # residual add fused with the norm
-        x = x + self.dropout(self.ffn(n2))
-        return x, new_state
+        return _ffn_residual(self, x, n2), new_state
 
 
 class _TitansLM(nn.Module):
@@ -173,7 +176,7 @@ class _TitansLM(nn.Module):
 
     def forward(self, input_ids: torch.Tensor, states: list[MemoryState] | None = None):
         h, new_states = self.hidden_states(input_ids, states)
-        return linear(h, self.head.weight), new_states
+        return linear(h, self.head.weight, use_kernels=self.config.use_kernels), new_states
 
 
 class TitansMAC(_TitansLM):

@@ -18,10 +18,17 @@ Reference semantics (``semantics="ref"``), as run by the reference on CUDA:
 * ``S' = eta*S - theta*G``,  ``W' = (1-alpha)*W + S'`` (`memory.py:464-498`).
 
 The deep-memory gradient is written out as explicit back-propagation through
-the MLP (no inner autograd graph), which is the same arithmetic the CUDA path
-runs as tcgen05/cuBLAS GEMMs with fused activation epilogues
-(``csrc/memory.cu``): every step stays on the device and the gates never
-leave it (no ``.item()`` host sync).
+the MLP (no inner autograd graph).  On CUDA (bf16) every GEMM of the update
+runs on the tcgen05 kernel of ``csrc/gemm_sm100.cu`` with the elementwise
+work in its epilogues: the hidden layers write ``z`` and ``act(z)``, the last
+layer writes the scaled error ``c (M(k) - v)``, the back-propagation GEMMs
+multiply by ``act'(z)``, and each weight-gradient GEMM (split-K over the
+B*T tokens, fixed-order sum) applies ``S' = eta S - theta G``,
+``W' = (1 - alpha) W + S'`` to the complete gradient with the gates read on
+the device -- the gradient itself is never stored, and nothing leaves the
+device (no ``.item()`` host sync).  The retrieval MLP (trainable) is one
+autograd node (:class:`_MemoryMLPFn`) with the activation in the forward
+GEMMs' epilogues and ``act'`` in the backward GEMMs' epilogues.
 """
 
 from __future__ import annotations
@@ -31,7 +38,9 @@ import math
 import torch
 import torch.nn.functional as F
 
+from . import gemm as G
 from ._ext import ext, want_kernels
+from .linear import _rows, kernel_ok, weight_grads
 
 
 def activation_fn(name: str):
@@ -46,7 +55,9 @@ def activation_fn(name: str):
 
 class _SiLU(torch.autograd.Function):
     """silu(z) on the extension's vectorised kernels: the forward keeps z, the
-    backward writes g * silu'(z) to a new tensor (one read of g and z, one write)."""
+    backward writes g * silu'(z) to a new tensor (one read of g and z, one write).
+    Gradients the kernel cannot take (dtype other than z's, unaligned) use the
+    PyTorch definition."""
 
     @staticmethod
     def forward(ctx, z):
@@ -56,12 +67,87 @@ class _SiLU(torch.autograd.Function):
         return a
 
     @staticmethod
+    @torch.autograd.function.once_differentiable
     def backward(ctx, g):
         (z,) = ctx.saved_tensors
         g = g.contiguous()
+        if g.dtype != z.dtype or g.data_ptr() % 16 != 0 or g.shape != z.shape:
+            return (g.float() * activation_grad("silu", z.float())).to(z.dtype)
         out = torch.empty_like(z)
         ext().act_grad_out(g, z, out, "silu")
         return out
+
+
+_ACT_KERNEL = ("silu", "gelu", "relu")
+
+
+class _MemoryMLPFn(torch.autograd.Function):
+    """The memory MLP ``W_L act(... act(W_1 x))`` as one autograd node on the tcgen05 GEMM:
+    forward GEMMs write ``z_i`` and ``act(z_i)``; the backward chains
+    ``dz_{i-1} = (dz_i W_i) * act'(z_{i-1})`` (the product in the GEMM epilogue),
+    ``dx = dz_1 W_1``, and the weight gradients ``dz_i^T h_{i-1}`` (in place
+    under the trainer)."""
+
+    @staticmethod
+    def forward(ctx, x, act, *weights):
+        x2 = _rows(x)
+        hs, zs = [x2], []
+        h = x2
+        L = len(weights)
+        for i, w in enumerate(weights):
+            if i < L - 1:
+                z, h = G.mm_act(h, w, act)
+                zs.append(z)
+                hs.append(h)
+            else:
+                h = G.mm_tn(h, w)
+        ctx.save_for_backward(*hs, *zs)
+        ctx.weights = weights
+        ctx.act = act
+        ctx.xshape = x.shape
+        return h.view(*x.shape[:-1], weights[-1].shape[0])
+
+    @staticmethod
+    def backward(ctx, dy):
+        weights, act = ctx.weights, ctx.act
+        L = len(weights)
+        saved = ctx.saved_tensors
+        hs, zs = saved[:L], saved[L:]
+        need = ctx.needs_input_grad[2:]
+        d = _rows(dy)
+        grads = [None] * L
+        dx = None
+        for i in range(L - 1, -1, -1):
+            nd = None
+            if i > 0:
+                nd = G.mm_act_grad(d, weights[i], zs[i - 1], act)
+            elif ctx.needs_input_grad[0]:
+                dx = G.mm_nn(d, weights[0]).view(ctx.xshape)
+            if need[i]:
+                (grads[i],) = weight_grads((weights[i],), d, hs[i], True, (True,))
+            d = nd
+        return (dx, None) + tuple(grads)
+
+
+def mlp_kernel_ok(x: torch.Tensor, weights, act: str, use_kernels: bool | None = None) -> bool:
+    """The fused tcgen05 memory-MLP path applies (bf16 CUDA, GEMM-compatible sizes)."""
+    if act not in _ACT_KERNEL or x.numel() == 0:
+        return False
+    if not kernel_ok(x, weights[0], use_kernels):
+        return False
+    return all(w.dtype == torch.bfloat16 and w.dim() == 2 and w.shape[0] % 8 == 0 and w.shape[1] % 8 == 0
+               for w in weights)
+
+
+def memory_mlp(x: torch.Tensor, weights, act: str) -> torch.Tensor:
+    """``MLP_W(x)`` on the fused tcgen05 path (callers check :func:`mlp_kernel_ok`)."""
+    if torch.is_grad_enabled() and (x.requires_grad or any(w.requires_grad for w in weights)):
+        return _MemoryMLPFn.apply(x, act, *weights)
+    x2 = _rows(x)
+    h = x2
+    for i, w in enumerate(weights):
+        h = G.mm_act(h, w, act, keep_z=False)[1] if i < len(weights) - 1 else G.mm_tn(h, w)
+    return h.view(*x.shape[:-1], weights[-1].shape[0])
 
 
 def activation(z: torch.Tensor, name: str, use_kernels: bool | None = None) -> torch.Tensor:
@@ -161,10 +247,49 @@ def memory_step(k: torch.Tensor, v: torch.Tensor, x_for_gates: torch.Tensor,
     return memory_update_reference(weights, momentum, grads, alpha, eta, theta)
 
 
+def _fused_update_ok(k2, v2, weights, momentum, act) -> bool:
+    if k2.dtype != torch.bfloat16 or v2.dtype != torch.bfloat16 or act not in _ACT_KERNEL:
+        return False
+    if not (G.operand_ok(k2) and G.operand_ok(v2)):
+        return False
+    for w, m in zip(weights, momentum, strict=True):
+        # the weights are GEMM operands (bf16); the momentum shares their dtype
+        if (w.dtype != torch.bfloat16 or m.dtype != w.dtype or w.dim() != 2 or not w.is_contiguous()
+                or not m.is_contiguous() or w.shape[0] % 8 or w.shape[1] % 8):
+            return False
+    return True
+
+
+def _memory_step_fused(k2, v2, weights, momentum, gates, act, linear_silu, B, T):
+    """The update on the tcgen05 GEMM: forward with act epilogues, error
+    epilogue, back-propagation with act' epilogues, and the gated update in
+    the epilogue of each (split-K) weight-gradient GEMM."""
+    L = len(weights)
+    if L == 1 and linear_silu:
+        h = torch.empty_like(k2)
+        ext().act_inplace(k2, h, act)
+        delta = G.mm_err(h, weights[0], v2, 2.0 / (B * T))
+        w2, m2 = G.mm_mem_update(delta, h, weights[0], momentum[0], gates)
+        return [w2], [m2]
+    hs, zs = [k2], []
+    h = k2
+    for i, w in enumerate(weights[:-1]):
+        z, h = G.mm_act(h, w, act)
+        zs.append(z)
+        hs.append(h)
+    delta = G.mm_err(h, weights[-1], v2, 2.0 / (k2.shape[0] * weights[-1].shape[0]))
+    new_w, new_m = [None] * L, [None] * L
+    for i in range(L - 1, -1, -1):
+        nd = G.mm_act_grad(delta, weights[i], zs[i - 1], act) if i > 0 else None  # old W_i
+        new_w[i], new_m[i] = G.mm_mem_update(delta, hs[i], weights[i], momentum[i], gates)
+        delta = nd
+    return new_w, new_m
+
+
 def _memory_step_cuda(k, v, x_for_gates, weights, momentum, gate_ws, gate_bs, lr, mom, act,
                       linear_silu):
-    """Device-resident update: gates kernel, cuBLAS GEMMs with fp32 weight-grad
-    output, activation/error epilogue kernels, fused momentum/decay update."""
+    """Device-resident update: gates kernel, then the fused tcgen05 path (bf16)
+    or PyTorch GEMMs with the extension's epilogue kernels."""
     E = ext()
     gates = E.memory_gates(x_for_gates, list(gate_ws), list(gate_bs), float(lr), float(mom))
     B, T, D = k.shape
@@ -174,6 +299,8 @@ def _memory_step_cuda(k, v, x_for_gates, weights, momentum, gate_ws, gate_bs, lr
         k2 = k2.contiguous()
     if not v2.is_contiguous():
         v2 = v2.contiguous()
+    if _fused_update_ok(k2, v2, weights, momentum, act) and want_kernels(k2):
+        return _memory_step_fused(k2, v2, list(weights), list(momentum), gates, act, linear_silu, B, T)
     L = len(weights)
     if L == 1 and linear_silu:
         h = torch.empty_like(k2)

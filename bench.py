@@ -234,12 +234,22 @@ def build_ours(device, world, parallel="dp"):
     return tr, nparams
 
 
-def build_reference(device, world, local):
+def build_reference(device, world, local, mode="as-shipped"):
     ref_dir = os.path.join(ROOT, "baseline", "_ref")
     if not os.path.isdir(os.path.join(ref_dir, "titans")):
         return None, "reference not installed under baseline/_ref"
     sys.path.insert(0, ref_dir)
     import titans  # the reference package, unmodified
+
+    if mode == "grad-correct":
+        # The shipped package calls raw Triton RMSNorm / SiLU-mul kernels without
+        # a backward on CUDA (src/titans/models.py:61-63, 105-111), so only the
+        # embedding trains.  Switching its Triton probe off before the first
+        # forward (a runtime flag, no source edit) makes it take its own PyTorch
+        # fallbacks: the same math as this framework's step, gradients included.
+        import titans.triton_kernels as tk
+
+        tk.HAS_TRITON = False
 
     torch.manual_seed(0)
     cls = {"mag": titans.TitansMAG, "mac": titans.TitansMAC, "mal": titans.TitansMAL}[CFG["model"]]
@@ -299,6 +309,9 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--ref-mode", choices=["as-shipped", "grad-correct"], default="as-shipped",
+                    help="reference arm: the package as shipped (its Triton RMSNorm / SiLU-mul cut the gradient, "
+                         "so only the embedding trains), or with its Triton probe off (full gradients)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--config", choices=sorted(CONFIGS), default="mag170m")
     ap.add_argument("--parallel", choices=["dp", "fsdp"], default="dp",
@@ -318,7 +331,7 @@ def main():
     K, W = args.steps, max(3, args.warmup)
 
     if args.impl == "reference":
-        built, why = build_reference(device, world, local)
+        built, why = build_reference(device, world, local, args.ref_mode)
         if built is None:
             if rank == 0:
                 print(json.dumps({"impl": "reference", "unavailable": why}))
@@ -401,7 +414,10 @@ def main():
         }
         if args.impl == "reference":
             out["impl"] = "reference"
-            out["reference_mode"] = ("as shipped: unmodified package, bf16 model (scripts/pretrain.py:460), "
+            out["reference_mode"] = (("as shipped" if args.ref_mode == "as-shipped" else
+                                      "gradient-correct (titans.triton_kernels.HAS_TRITON = False at run time: "
+                                      "PyTorch RMSNorm / SiLU-mul with gradients)")
+                                     + ": unmodified package, bf16 model (scripts/pretrain.py:460), "
                                      "fused AdamW, clip 1.0; for N>1 grads averaged by one flat NCCL all-reduce "
                                      "after backward (its DDP raises or stalls)"
                                      + ("; activation checkpointing off (the reference's own "

@@ -296,3 +296,22 @@ def test_silu_activation_kernel(dtype, shape):
     a.backward(g.to(dtype))
     ar.backward(g)
     assert rel_err(z.grad, zr.grad) < 1e-2
+
+
+@pytest.mark.gpu
+def test_exp2_poly_error_bound():
+    """The attention softmax's FMA-pipe 2^x (cubic on the fraction, exponent by
+    integer add) against exp2: relative error within the stated 1.1e-4 on
+    [-125, 0], and 0 below -125."""
+    from titans_pytorch_b200.ops import _ext
+
+    E = _ext.ext()
+    x = torch.linspace(-125.0, 0.0, 2_000_001, device="cuda", dtype=torch.float32)
+    y = E.exp2_poly_eval(x)
+    ref = torch.exp2(x.double())
+    rel = ((y.double() - ref).abs() / ref).max().item()
+    assert rel <= 1.1e-4, rel
+    rel_cuda = ((y - torch.exp2(x)).abs() / torch.exp2(x)).max().item()  # CUDA's own exp2f
+    assert rel_cuda <= 1.2e-4, rel_cuda
+    below = E.exp2_poly_eval(torch.tensor([-126.0, -1e4, -float("inf")], device="cuda"))
+    assert torch.all(below == 0)

@@ -7,6 +7,8 @@ this exported C symbol with their own input and output buffers; its scratch
 space is a fixed device array inside the library.  These tests call it through
 ctypes and compare it with the library's PyTorch-facing ``rms_norm_bwd`` on two
 calls in a row (the shared scratch array must not leak state between calls).
+Each call is also checked against an fp32 PyTorch restatement of the RMSNorm
+backward, so the test does not rest on the other entry point alone.
 This file is named so that pytest collects it last.
 """
 
@@ -50,6 +52,17 @@ def rel_err(a, b):
     return float((a - b).norm() / (b.norm() + 1e-12))
 
 
+def rms_bwd_fp32(dy, x, w, eps=1e-6):
+    """fp32 restatement: y = x * r * w with r = (mean(x^2) + eps)^-1/2."""
+    x, dy, w = x.float(), dy.float(), w.float()
+    r = torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + eps)
+    xh = x * r
+    g = dy * w
+    dx = r * (g - xh * (g * xh).mean(-1, keepdim=True))
+    dw = (dy * xh).sum(0)
+    return dx, dw
+
+
 @pytest.mark.parametrize("dtype,rows,dim", [(torch.bfloat16, 4096, 768), (torch.bfloat16, 37, 1536),
                                              (torch.float32, 300, 1024), (torch.bfloat16, 5, 4096)])
 def test_noalloc_matches_torch_entry_point_twice(dtype, rows, dim):
@@ -70,6 +83,9 @@ def test_noalloc_matches_torch_entry_point_twice(dtype, rows, dim):
         assert rc == OK
         assert rel_err(dx, dx_ref) < tol
         assert rel_err(dw, dw_ref) < tol
+        dx32, dw32 = rms_bwd_fp32(dy, x, w)
+        assert rel_err(dx, dx32) < tol
+        assert rel_err(dw, dw32) < tol
 
 
 def test_noalloc_rejects_sizes_beyond_the_maximum():

@@ -128,6 +128,18 @@ __device__ __forceinline__ void exp2_poly2(float x0, float x1, float& y0, float&
   y1 = x1 < -125.f ? 0.f : __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23));
 }
 
+// Test hook: y = exp2_poly2(x) elementwise (pairs), so the polynomial's error
+// bound can be checked directly against exp2 on the device.
+__global__ void exp2_poly_eval_kernel(const float* __restrict__ x, float* __restrict__ y, int64_t n) {
+  const int64_t i = 2 * ((int64_t)blockIdx.x * blockDim.x + threadIdx.x);
+  if (i + 1 < n) {
+    exp2_poly2(x[i], x[i + 1], y[i], y[i + 1]);
+  } else if (i < n) {
+    float dummy;
+    exp2_poly2(x[i], 0.f, y[i], dummy);
+  }
+}
+
 // tmQ/tmK/tmV: columns 0-63 (128-byte swizzle); tmQb/tmKb/tmVb: columns 64-95
 // (64-byte swizzle), used when HD = 96.
 template <int HD>
@@ -509,6 +521,18 @@ at::Tensor& tc_error_word(const at::Device& dev) {
   at::Tensor& w = words.at(dev.index());
   if (!w.defined()) w = at::zeros({1}, at::TensorOptions().device(dev).dtype(at::kInt));
   return w;
+}
+
+at::Tensor exp2_poly_eval(const at::Tensor& x) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kFloat, "exp2_poly_eval: fp32 CUDA tensor");
+  const at::cuda::CUDAGuard g(x.device());
+  at::Tensor xc = x.contiguous();
+  at::Tensor y = at::empty_like(xc);
+  const int64_t n = xc.numel();
+  if (n) attn_tc::exp2_poly_eval_kernel<<<(unsigned)((n / 2 + 255) / 256 + 1), 256, 0, stream()>>>(
+             xc.data_ptr<float>(), y.data_ptr<float>(), n);
+  check_launch("exp2_poly_eval");
+  return y;
 }
 
 int64_t kernel_error_status(int64_t device, bool reset) {

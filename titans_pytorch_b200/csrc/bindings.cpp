@@ -18,6 +18,7 @@ std::vector<at::Tensor> conv_silu_norm_bwd(const at::Tensor& dy, const at::Tenso
 // elementwise.cu
 at::Tensor swiglu_fwd(const at::Tensor& gu);
 at::Tensor swiglu_bwd(const at::Tensor& dh, const at::Tensor& gu);
+at::Tensor silu_mul(const at::Tensor& g, const at::Tensor& u);
 at::Tensor memory_gates(const at::Tensor& x, const std::vector<at::Tensor>& ws, const std::vector<at::Tensor>& bs,
                         double lr, double mom);
 void act_inplace(const at::Tensor& z, at::Tensor& a, const std::string& act);
@@ -58,6 +59,7 @@ std::vector<at::Tensor> attn_bwd_tc(const at::Tensor& dO, const at::Tensor& Q, c
                                     const at::Tensor& V, const at::Tensor& O, const at::Tensor& LSE, int64_t window,
                                     double scale);
 int64_t kernel_error_status(int64_t device, bool reset);
+at::Tensor exp2_poly_eval(const at::Tensor& x);
 at::Tensor memory_scan_fwd(at::Tensor& W1, at::Tensor& S1, at::Tensor& W2T, at::Tensor& S2T, const at::Tensor& k,
                            const at::Tensor& v, const at::Tensor& q, const at::Tensor& theta, const at::Tensor& eta,
                            const at::Tensor& alpha);
@@ -66,7 +68,7 @@ std::vector<at::Tensor> comm_alloc(int64_t nbytes, int64_t device);
 int64_t comm_ipc_open(const at::Tensor& handle, int64_t device);
 void comm_ipc_close(int64_t ptr);
 void comm_barrier(const at::Tensor& sig_ptrs, int64_t slot, at::Tensor& epoch, bool bump, int64_t world, int64_t me,
-                  at::Tensor& err);
+                  at::Tensor& err, int64_t budget);
 void comm_reduce_shard(const at::Tensor& grad_ptrs, int64_t lo, int64_t n, at::Tensor& gsum, double gscale,
                        const at::Tensor& slot_ptrs, int64_t world, int64_t me);
 void comm_adamw_shard(const at::Tensor& gsum, at::Tensor& master, at::Tensor& exp_avg, at::Tensor& exp_avg_sq,
@@ -98,6 +100,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("conv_silu_norm_bwd", &tb::conv_silu_norm_bwd);
   m.def("swiglu_fwd", &tb::swiglu_fwd);
   m.def("swiglu_bwd", &tb::swiglu_bwd);
+  m.def("silu_mul", &tb::silu_mul);
   m.def("memory_gates", &tb::memory_gates);
   m.def("act_inplace", &tb::act_inplace);
   m.def("act_grad_mul", &tb::act_grad_mul);
@@ -125,7 +128,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("comm_alloc", &tb::comm_alloc);
   m.def("comm_ipc_open", &tb::comm_ipc_open);
   m.def("comm_ipc_close", &tb::comm_ipc_close);
-  m.def("comm_barrier", &tb::comm_barrier);
+  m.def("comm_barrier", &tb::comm_barrier, pybind11::arg("sig_ptrs"), pybind11::arg("slot"), pybind11::arg("epoch"),
+        pybind11::arg("bump"), pybind11::arg("world"), pybind11::arg("me"), pybind11::arg("err"),
+        pybind11::arg("budget") = (int64_t)1 << 31);
   m.def("comm_reduce_shard", &tb::comm_reduce_shard);
   m.def("comm_adamw_shard", &tb::comm_adamw_shard, pybind11::arg("gsum"), pybind11::arg("master"),
         pybind11::arg("exp_avg"), pybind11::arg("exp_avg_sq"), pybind11::arg("param_ptrs"), pybind11::arg("lo"),
@@ -144,5 +149,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         pybind11::arg("R2") = pybind11::none(), pybind11::arg("gates") = pybind11::none(),
         pybind11::arg("scale") = 1.0, pybind11::arg("act") = 0, pybind11::arg("ffn_f") = 0,
         pybind11::arg("splits") = 0);
+  m.def("exp2_poly_eval", &tb::exp2_poly_eval);
   m.def("kernel_error_status", &tb::kernel_error_status, pybind11::arg("device") = 0, pybind11::arg("reset") = true);
 }

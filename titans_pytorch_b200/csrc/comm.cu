@@ -39,7 +39,7 @@ __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
 // one block of `world` (>= 32 rounded) threads; epoch = *epoch_dev (+1, stored
 // back, when `bump`)
 __global__ void barrier_kernel(uint32_t* const* __restrict__ sig_ptrs, int slot, uint32_t* __restrict__ epoch_dev,
-                               int bump, int world, int me, unsigned* __restrict__ err) {
+                               int bump, int world, int me, unsigned* __restrict__ err, long long budget) {
   const int t = threadIdx.x;
   __shared__ uint32_t ep;
   if (t == 0) {
@@ -54,7 +54,7 @@ __global__ void barrier_kernel(uint32_t* const* __restrict__ sig_ptrs, int slot,
     const uint32_t* mine = sig_ptrs[me] + slot * world + t;
     const long long t0 = clock64();
     while (ld_acquire_sys(mine) < epoch) {
-      if (clock64() - t0 > (1ll << 31)) {
+      if (clock64() - t0 > budget) {
         atomicCAS(err, 0u, 100u + (unsigned)slot);
         break;
       }
@@ -250,13 +250,16 @@ void comm_ipc_close(int64_t ptr) {
   if (ptr) C10_CUDA_CHECK(cudaIpcCloseMemHandle((void*)(uintptr_t)ptr));
 }
 
+// `budget`: clock cycles each wait may spin before it records 100 + slot in
+// `err` and returns (default 2^31, about a second).
 void comm_barrier(const at::Tensor& sig_ptrs, int64_t slot, at::Tensor& epoch, bool bump, int64_t world, int64_t me,
-                  at::Tensor& err) {
+                  at::Tensor& err, int64_t budget) {
   TORCH_CHECK(epoch.is_cuda() && epoch.scalar_type() == at::kInt && epoch.numel() == 1, "comm_barrier: epoch word");
+  TORCH_CHECK(budget > 0, "comm_barrier: budget must be positive");
   comm::barrier_kernel<<<1, 32 * ((world + 31) / 32), 0, stream()>>>(
       reinterpret_cast<uint32_t* const*>(sig_ptrs.data_ptr<int64_t>()), (int)slot,
       reinterpret_cast<uint32_t*>(epoch.data_ptr<int>()), bump ? 1 : 0, (int)world, (int)me,
-      (unsigned*)err.data_ptr<int>());
+      (unsigned*)err.data_ptr<int>(), (long long)budget);
   check_launch("comm_barrier");
 }
 

@@ -7,17 +7,19 @@
 namespace tb {
 
 // ---------------------------------------------------------------- SwiGLU
-// gu: [M, 2F] = [gate | up] ; h = silu(gate) * up : [M, F]
+// h = silu(gate) * up : [M, F]; gate row m at g + m * ldg, up row m at u + m * ldu
+// (the stacked gu [M, 2F] = [gate | up] is g = gu, u = gu + F, ld = 2F)
 template <typename T>
-__global__ void swiglu_fwd_kernel(const T* __restrict__ gu, T* __restrict__ h, int64_t M, int F) {
+__global__ void swiglu_fwd_kernel(const T* __restrict__ gp, int64_t ldg, const T* __restrict__ up, int64_t ldu,
+                                  T* __restrict__ h, int64_t M, int F) {
   constexpr int V = Vec16<T>::N;
   const int64_t nvec = M * (F / V);
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nvec; i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t m = i / (F / V);
     const int c = (int)(i % (F / V)) * V;
     float g[V], u[V], o[V];
-    load16<T>(gu + m * 2 * F + c, g);
-    load16<T>(gu + m * 2 * F + F + c, u);
+    load16<T>(gp + m * ldg + c, g);
+    load16<T>(up + m * ldu + c, u);
 #pragma unroll
     for (int k = 0; k < V; ++k) o[k] = silu_(g[k]) * u[k];
     store16<T>(h + m * F + c, o);
@@ -61,9 +63,32 @@ at::Tensor swiglu_fwd(const at::Tensor& gu) {
     constexpr int V = Vec16<scalar_t>::N;
     TORCH_CHECK(F % V == 0, "swiglu: F must be a multiple of ", V);
     const int64_t n = M * (F / V);
-    if (n) swiglu_fwd_kernel<scalar_t><<<ew_blocks(n), 256, 0, stream()>>>((const scalar_t*)x.data_ptr(), (scalar_t*)h.data_ptr(), M, F);
+    const scalar_t* gp = (const scalar_t*)x.data_ptr();
+    if (n) swiglu_fwd_kernel<scalar_t><<<ew_blocks(n), 256, 0, stream()>>>(gp, 2 * F, gp + F, 2 * F,
+                                                                            (scalar_t*)h.data_ptr(), M, F);
   });
   check_launch("swiglu_fwd");
+  return h;
+}
+
+// h = silu(g) * u for two same-shape tensors (any leading shape, flattened)
+at::Tensor silu_mul(const at::Tensor& g, const at::Tensor& u) {
+  TB_CHECK_CUDA(g);
+  TORCH_CHECK(g.sizes() == u.sizes() && g.scalar_type() == u.scalar_type(), "silu_mul: same shape and dtype");
+  const at::cuda::CUDAGuard guard(g.device());
+  at::Tensor gc = contig16(g), uc = contig16(u);
+  at::Tensor h = at::empty_like(gc);
+  const int64_t F = gc.dim() ? gc.size(-1) : 1;
+  const int64_t M = F ? gc.numel() / F : 0;
+  TB_DISPATCH_FLOAT(gc.scalar_type(), "silu_mul", [&] {
+    constexpr int V = Vec16<scalar_t>::N;
+    TORCH_CHECK(F % V == 0, "silu_mul: the last dim must be a multiple of ", V);
+    const int64_t n = M * (F / V);
+    if (n) swiglu_fwd_kernel<scalar_t><<<ew_blocks(n), 256, 0, stream()>>>(
+               (const scalar_t*)gc.data_ptr(), F, (const scalar_t*)uc.data_ptr(), F, (scalar_t*)h.data_ptr(), M,
+               (int)F);
+  });
+  check_launch("silu_mul");
   return h;
 }
 

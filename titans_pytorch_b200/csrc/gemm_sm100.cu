@@ -1,5 +1,5 @@
 // Host side of the 2-CTA tcgen05 GEMM (kernels in gemm_sm100.cuh, specialised
-// per operand layout in gemm_sm100_k.cu / gemm_sm100_mn.cu) and the split-K
+// per operand layout and tile width in gemm_sm100_k256.cu / _k128.cu / _mn.cu) and the split-K
 // reduction kernel.
 #include "gemm_sm100.cuh"
 
@@ -108,7 +108,7 @@ __device__ __forceinline__ void epi8(const Args& p, int64_t m, int n, const floa
 // One thread per 8 columns of one accumulator row: sums the `splits`
 // partials (split 0 first) from the workspace and runs the epilogue.
 __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restrict__ ws, const Args p) {
-  constexpr int CH = BN / 8;
+  const int BN = p.bn, CH = BN / 8;
   const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const int64_t total = (int64_t)p.tiles * BM * CH;
   if (idx >= total) return;
@@ -274,10 +274,19 @@ void gemm_sm100(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn, 
   a.N = (int)N;
   a.K = (int)K;
   a.n_mt = (int)((M + BM - 1) / BM);
-  a.n_nt = swiglu ? (int)((ffn_f + BN / 2 - 1) / (BN / 2)) : (int)((N + BN - 1) / BN);
-  a.tiles = a.n_mt * a.n_nt;
   a.kb_total = (int)((K + BK - 1) / BK);
   const int ncl = std::max(1, num_sms() / 2);
+  // 256 x 256 tiles, or 256 x 128 when the 256-wide tiles would leave CTA
+  // pairs idle in a single partial wave and halving them fills more of the GPU
+  // (weight gradients, both operands MN-major, fill the GPU with split-K instead)
+  const auto n_tiles = [&](int bn) {
+    return a.n_mt * (swiglu ? (int)((ffn_f + bn / 2 - 1) / (bn / 2)) : (int)((N + bn - 1) / bn));
+  };
+  int BN = 256;
+  if (!(a_mn && b_mn) && n_tiles(256) < ncl && n_tiles(128) > n_tiles(256)) BN = 128;
+  a.bn = BN;
+  a.n_nt = swiglu ? (int)((ffn_f + BN / 2 - 1) / (BN / 2)) : (int)((N + BN - 1) / BN);
+  a.tiles = a.n_mt * a.n_nt;
   const bool split_ok = !swiglu;
   int s = (int)splits;
   const bool partial_anyway = !(mode == STORE || mode == RESID || mode == ACT || mode == ERR || mode == ACT_GRAD);
@@ -353,8 +362,12 @@ void gemm_sm100(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn, 
     mp.ws = epi_map(ws, BN, (uint64_t)a.items * 2 * HM);
   }
   cudaStream_t st = stream();
-#define TB_G2(AM, BMN, MD) \
-  if (a_mn == AM && b_mn == BMN && kmode == MD) { launch_gemm2<AM, BMN, MD>(mp, a, st); goto launched; }
+#define TB_G2(AM, BMN, MD)                                                          \
+  if (a_mn == AM && b_mn == BMN && kmode == MD) {                                     \
+    if (BN == 256) launch_gemm2<AM, BMN, MD, 256>(mp, a, st);                         \
+    else launch_gemm2<AM, BMN, MD, 128>(mp, a, st);                                   \
+    goto launched;                                                                    \
+  }
   TB_G2(false, false, STORE) TB_G2(false, false, RESID) TB_G2(false, false, ACT) TB_G2(false, false, ERR)
   TB_G2(false, false, SWIGLU) TB_G2(false, false, PARTIAL)
   TB_G2(false, true, STORE) TB_G2(false, true, ACT_GRAD) TB_G2(false, true, SWIGLU_BWD) TB_G2(false, true, PARTIAL)

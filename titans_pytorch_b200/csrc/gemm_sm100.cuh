@@ -80,11 +80,11 @@ namespace g2 {
 
 constexpr int HM = 128;       // accumulator rows per CTA
 constexpr int BM = 2 * HM;    // tile rows per CTA pair
-constexpr int BN = 256;       // tile columns
+constexpr int BN_MAX = 256;   // tile columns: 256, or 128 for problems too small to fill the GPU
 constexpr int BK = 64;        // k-slice per stage (128 bytes of bf16)
 constexpr int NTHREADS = 192;
 constexpr int EPI_WARP0 = 2;
-constexpr int TM_COLS = 512;  // two accumulators of BN columns
+constexpr int TM_COLS = 512;  // two accumulators of up to 256 columns
 constexpr int STG_WARP = 16384;  // epilogue staging per warp: two sets of 8 KB
 
 enum Mode : int {
@@ -98,6 +98,7 @@ struct Args {
   int n_mt, n_nt, tiles, splits, kb_total, kb_per_split, items;
   int b_nstep, b_rstep;  // B-half row origin = nt * b_nstep + rank * b_rstep
   int mode, act, ffn_f, state_f32;
+  int bn;  // tile columns (the kernel's BN; read by the split-K reduction)
   float scale;
   void* c;
   int64_t ldc;
@@ -121,6 +122,7 @@ struct Maps {
   CUtensorMap a, b, c, c2, r, r2, ws;
 };
 
+template <int BN>
 struct Cfg {
   static constexpr int A_BYTES = HM * BK * 2;
   static constexpr int B_BYTES = (BN / 2) * BK * 2;
@@ -388,11 +390,11 @@ __device__ __forceinline__ void issue_in(const Maps& mp, int ffn_f, uint8_t* sb,
 }
 
 // Output column of epilogue step c of tile column nt, and the step count.
-template <int MODE>
+template <int MODE, int BN>
 __device__ __forceinline__ int step_col(int nt, int c) {
   return MODE == SWIGLU ? nt * (BN / 2) + c * 32 : nt * BN + c * step_cols<MODE>();
 }
-template <int MODE>
+template <int MODE, int BN>
 __device__ __forceinline__ int step_count(const Args& p, int nt) {
   constexpr int SC = step_cols<MODE>();
   if constexpr (MODE == SWIGLU) return min(BN / 64, (p.ffn_f - nt * (BN / 2) + 31) / 32);
@@ -418,10 +420,10 @@ __device__ __forceinline__ void ld_row128(const uint8_t* blk, int r, uint32_t (&
   }
 }
 
-template <bool A_MN, bool B_MN, int MODE>
+template <bool A_MN, bool B_MN, int MODE, int BN>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
     gemm2_kernel(const __grid_constant__ Maps mp, const Args p) {
-  using C = Cfg;
+  using C = Cfg<BN>;
   constexpr int NS = C::NS;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -562,9 +564,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
         tile_of(p, pf_item, pmt, pnt, psp);
         const int prow0 = pmt * BM + (int)rank * HM + q * 32;
         const int slot = pf_k % NSLOT;
-        issue_in<MODE>(mp, ffn_f, stg + slot * SLOT, step_col<MODE>(pnt, pf_c), prow0, bl + slot);
+        issue_in<MODE>(mp, ffn_f, stg + slot * SLOT, step_col<MODE, BN>(pnt, pf_c), prow0, bl + slot);
         ++pf_k;
-        if (++pf_c == step_count<MODE>(p, pnt)) {
+        if (++pf_c == step_count<MODE, BN>(p, pnt)) {
           pf_c = 0;
           pf_item += ncl;
         }
@@ -580,7 +582,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
       tile_of(p, item, mt, nt, split);
       const int buf = li & 1;
       const int row0 = mt * BM + (int)rank * HM + q * 32;
-      const int nsteps = step_count<MODE>(p, nt);
+      const int nsteps = step_count<MODE, BN>(p, nt);
       if (!tc::mbar_wait(bar_acc_full + buf, (li >> 1) & 1, abort_flag, p.err)) break;
       tc::tc_fence_after();
       const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + buf * BN;
@@ -588,7 +590,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
       for (int c = 0; c < nsteps; ++c, ++step) {
         const int slot = step % NSLOT;
         uint8_t* sb = stg + slot * SLOT;
-        const int n = step_col<MODE>(nt, c);
+        const int n = step_col<MODE, BN>(nt, c);
         if constexpr (in_bytes<MODE>() == 0) {
           // the stores that last used this slot (NSLOT steps ago) have read it
           if (lane == 0) bulk_wait_read<NSLOT - 1>();
@@ -732,20 +734,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
 }
 
 // Launch of one specialisation (defined in the per-layout translation units).
-template <bool A_MN, bool B_MN, int MODE>
+template <bool A_MN, bool B_MN, int MODE, int BN>
 void launch_gemm2(const Maps& mp, const Args& a, cudaStream_t st);
 
 // Grid: one CTA pair per co-resident cluster slot (at most SMs / 2), at most one per work item.
-template <bool A_MN, bool B_MN, int MODE>
+template <bool A_MN, bool B_MN, int MODE, int BN>
 void launch_gemm2_impl(const Maps& mp, const Args& a, cudaStream_t st) {
   static int ncl_max = -1;
-  auto kern = gemm2_kernel<A_MN, B_MN, MODE>;
+  using C = Cfg<BN>;
+  auto kern = gemm2_kernel<A_MN, B_MN, MODE, BN>;
   if (ncl_max < 0) {
-    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
+    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * (num_sms() / 2));
     cfg.blockDim = dim3(NTHREADS);
-    cfg.dynamicSmemBytes = Cfg::SMEM;
+    cfg.dynamicSmemBytes = C::SMEM;
     int c = 0;
     if (cudaOccupancyMaxActiveClusters(&c, kern, &cfg) != cudaSuccess || c <= 0) {
       cudaGetLastError();
@@ -754,7 +757,7 @@ void launch_gemm2_impl(const Maps& mp, const Args& a, cudaStream_t st) {
     ncl_max = std::min(c, num_sms() / 2);
   }
   const int ncl = std::min(a.items, ncl_max);
-  kern<<<2 * ncl, NTHREADS, Cfg::SMEM, st>>>(mp, a);
+  kern<<<2 * ncl, NTHREADS, C::SMEM, st>>>(mp, a);
 }
 
 }  // namespace g2

@@ -26,9 +26,15 @@ int g_num_sms[kMaxDevices];
 std::mutex g_setup_mutex;
 
 // Once per device, with that device current: resolve the scratch address.
-int setup_device(int dev) {
+// The address and SM count are handed back while the lock is held, so no
+// caller reads the per-device tables unsynchronised.
+int setup_device(int dev, float** scratch, int* nsm) {
   std::lock_guard<std::mutex> lock(g_setup_mutex);
-  if (g_scratch_ptr[dev] != nullptr) return TITANS_NOALLOC_OK;
+  if (g_scratch_ptr[dev] != nullptr) {
+    *scratch = g_scratch_ptr[dev];
+    *nsm = g_num_sms[dev];
+    return TITANS_NOALLOC_OK;
+  }
   void* p = nullptr;
   if (cudaGetSymbolAddress(&p, g_rms_bwd_scratch) != cudaSuccess || p == nullptr) {
     cudaGetLastError();
@@ -41,6 +47,8 @@ int setup_device(int dev) {
   }
   g_num_sms[dev] = n;
   g_scratch_ptr[dev] = static_cast<float*>(p);
+  *scratch = g_scratch_ptr[dev];
+  *nsm = n;
   return TITANS_NOALLOC_OK;
 }
 
@@ -98,7 +106,9 @@ extern "C" int titans_rms_norm_bwd_noalloc(const void* dy, const void* x, const 
     cudaGetLastError();
     return TITANS_NOALLOC_EINVAL;
   }
-  const int rc = setup_device(dev);
+  float* scratch = nullptr;
+  int nsm = 0;
+  const int rc = setup_device(dev, &scratch, &nsm);
   if (rc != TITANS_NOALLOC_OK) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (rows == 0) {
@@ -106,9 +116,8 @@ extern "C" int titans_rms_norm_bwd_noalloc(const void* dy, const void* x, const 
                                                                                        : TITANS_NOALLOC_ELAUNCH;
   }
   // same block count as the PyTorch entry point, capped so the partials fit the scratch array
-  int64_t blocks = std::min<int64_t>((rows + 7) / 8, (int64_t)g_num_sms[dev] * 2);
+  int64_t blocks = std::min<int64_t>((rows + 7) / 8, (int64_t)nsm * 2);
   blocks = std::max<int64_t>(1, std::min<int64_t>(blocks, kScratchFloats / dim));
-  float* scratch = g_scratch_ptr[dev];
   if (dtype == TITANS_DTYPE_BF16)
     return dispatch<__nv_bfloat16>(chn, dy, x, weight, rstd, dx, dweight, rows, dim, (int)blocks, scratch, st);
   return dispatch<float>(chn, dy, x, weight, rstd, dx, dweight, rows, dim, (int)blocks, scratch, st);

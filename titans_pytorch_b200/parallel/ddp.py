@@ -71,6 +71,9 @@ class _PeerBuffer:
 class FusedDPAdamW(FusedAdamW):
     """ZeRO-1 AdamW whose step is the fused peer-memory reduce + update + all-gather."""
 
+    # each rank holds only its shard of the optimizer state: checkpoints keep one file per rank
+    shard_state = True
+
     def __init__(self, model: torch.nn.Module, cfg, group=None, device=None):
         self.group = group
         self.world = dist.get_world_size(group)

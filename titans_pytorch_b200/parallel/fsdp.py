@@ -118,6 +118,9 @@ class ShardLayout:
 class FSDPAdamW(FusedAdamW):
     """AdamW over per-block parameter shards; see the module docstring."""
 
+    # each rank holds only its shard of the optimizer state: checkpoints keep one file per rank
+    shard_state = True
+
     def __init__(self, model: nn.Module, cfg, group=None, fused: bool = True):
         self.group = group
         self.world = dist.get_world_size(group)

@@ -182,17 +182,35 @@ class Trainer:
         self.global_step += 1
 
     @torch.no_grad()
-    def evaluate(self, batches) -> dict[str, float]:
+    def evaluate(self, batches, group=None, max_batches: int | None = None) -> dict[str, float]:
+        """Mean token loss over ``batches`` (and, in a process group, over every
+        rank's batches: the (loss sum, token count) pair is all-reduced, as the
+        reference gathers its eval losses, `scripts/pretrain_distributed.py:479-518`).
+        Sums stay on the device until the end (one host read)."""
+        import torch.distributed as dist
+
         self.model.eval()
-        tot, n = 0.0, 0
-        for b in batches:
+        acc = torch.zeros(2, dtype=torch.float64, device=self.device)
+        for i, b in enumerate(batches):
+            if max_batches is not None and i >= max_batches:
+                break
             ids = self._to_device(b["input_ids"])
             labels = self._to_device(b["labels"])
             logits, _ = self.model(ids)
-            loss = cross_entropy(logits, labels)
-            k = int((labels != -100).sum())
-            tot += float(loss) * k
-            n += k
+            loss = cross_entropy(logits, labels, use_kernels=getattr(self.model.config, "use_kernels", None))
+            k = (labels != -100).sum()
+            acc[0] += loss.double() * k
+            acc[1] += k
         self.model.train()
-        avg = tot / max(n, 1)
-        return {"val_loss": avg, "val_ppl": math.exp(min(avg, 20.0))}
+        if dist.is_available() and dist.is_initialized():
+            dist.all_reduce(acc, group=group)
+        tot, n = acc.tolist()
+        avg = tot / max(n, 1.0)
+        return {"val_loss": avg, "val_ppl": math.exp(min(avg, 20.0)), "val_tokens": int(n)}
+
+    def check_errors(self) -> None:
+        """Raise if a bounded device wait of this trainer's kernels ran out
+        (see :mod:`titans_pytorch_b200.parallel.health`); synchronises."""
+        from ..parallel.health import check_device_errors
+
+        check_device_errors(self.optimizer, self.device if self.device.type == "cuda" else None)

@@ -60,7 +60,8 @@ def set_rng_state(st: dict[str, Any]) -> None:
 def save_checkpoint(path: str, model: torch.nn.Module, optimizer=None, scheduler=None, *, global_step: int = 0,
                     epoch: int = 0, best_val_loss: float = float("inf"), model_type: str | None = None,
                     tokenizer_name: str | None = None, data_position: int | None = None,
-                    train_config: dict | None = None, dtype: torch.dtype | None = None) -> str:
+                    train_config: dict | None = None, dtype: torch.dtype | None = None,
+                    extra: dict | None = None) -> str:
     """Write a reference-loadable checkpoint (plus resume state) to ``path``."""
     cfg: TitansConfig = model.config
     sd = {k: (v.to(dtype) if dtype is not None and v.is_floating_point() else v).detach().cpu()
@@ -82,11 +83,70 @@ def save_checkpoint(path: str, model: torch.nn.Module, optimizer=None, scheduler
     }
     if tokenizer_name is not None:
         ckpt["tokenizer_name"] = tokenizer_name
+    if extra:
+        ckpt.update(extra)
+    _atomic_save(ckpt, path)
+    return path
+
+
+def _atomic_save(obj, path: str) -> None:
     os.makedirs(os.path.dirname(os.path.abspath(path)), exist_ok=True)
     tmp = path + ".tmp"
-    torch.save(ckpt, tmp)
+    torch.save(obj, tmp)
     os.replace(tmp, path)  # never leave a truncated checkpoint behind
+
+
+def shard_path(path: str, rank: int, world: int) -> str:
+    """File holding rank ``rank``'s optimizer shard of checkpoint ``path``."""
+    return f"{path}.optim.rank{rank}-of-{world}"
+
+
+def _barrier(group=None) -> None:
+    import torch.distributed as dist
+
+    if dist.is_available() and dist.is_initialized():
+        dist.barrier(group=group)
+
+
+def save_training_checkpoint(path: str, trainer, *, rank: int = 0, world: int = 1, group=None, **meta) -> str:
+    """Checkpoint of a (possibly data-parallel) training run; EVERY rank calls it.
+
+    Parameters still sharded are gathered first.  An optimizer whose state is
+    sharded over the ranks (``shard_state``) writes one file per rank
+    (:func:`shard_path`) and rank 0 writes the reference-loadable model file
+    with ``optimizer_shards = world``; otherwise rank 0 writes everything.  A
+    host barrier at the end keeps every rank out of the next step until all
+    files are on disk (the fused data-parallel step's device barriers have a
+    time budget, and a long write on rank 0 must not run it out)."""
+    opt = trainer.optimizer
+    mat = getattr(opt, "materialize", None)
+    if mat is not None:
+        mat()
+    sharded = world > 1 and getattr(opt, "shard_state", False)
+    if sharded:
+        sd = {k: (v.detach().cpu() if isinstance(v, torch.Tensor) else v) for k, v in opt.state_dict().items()}
+        _atomic_save(sd, shard_path(path, rank, world))
+    if rank == 0:
+        save_checkpoint(path, trainer.model, None if sharded else opt, trainer.scheduler,
+                        extra={"optimizer_shards": world if sharded else 0}, **meta)
+    _barrier(group)
     return path
+
+
+def load_training_checkpoint(path: str, trainer, *, rank: int = 0, world: int = 1, restore_rng: bool = True) -> dict:
+    """Restore :func:`save_training_checkpoint` output on every rank (weights,
+    scheduler, RNG, and this rank's optimizer shard or the full optimizer)."""
+    ckpt = load_checkpoint(path, trainer.model, None, trainer.scheduler, restore_rng=restore_rng)
+    opt = trainer.optimizer
+    shards = int(ckpt.get("optimizer_shards") or 0)
+    if shards:
+        if shards != world:
+            raise ValueError(f"{path}: optimizer saved over {shards} ranks, resuming on {world}")
+        sd = torch.load(shard_path(path, rank, world), map_location="cpu", weights_only=False)
+        opt.load_state_dict(sd)
+    elif ckpt.get("optimizer_state_dict") is not None:
+        opt.load_state_dict(ckpt["optimizer_state_dict"])
+    return ckpt
 
 
 def load_model(path: str, device=None, dtype: torch.dtype | None = None, **config_overrides):

@@ -256,7 +256,18 @@ from ..ops.norm import fused_add_rms_norm  # noqa: E402  (kernel-backed residual
 
 
 def fused_silu_mul(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
-    """silu(gate) * up."""
+    """silu(gate) * up: one elementwise kernel on CUDA (the reference's
+    `cuda_optimizations.py:118-125` is two PyTorch ops).  Tensors that need a
+    gradient, or that the kernel cannot take, use the PyTorch definition."""
+    from ..ops._ext import want_kernels
+
+    if (want_kernels(gate) and gate.shape == up.shape and gate.dtype == up.dtype
+            and gate.dtype in (torch.bfloat16, torch.float16, torch.float32)
+            and gate.shape[-1] % (16 // gate.element_size()) == 0
+            and not (torch.is_grad_enabled() and (gate.requires_grad or up.requires_grad))):
+        from ..ops._ext import ext
+
+        return ext().silu_mul(gate, up)
     return torch.nn.functional.silu(gate) * up
 
 

@@ -1,5 +1,5 @@
 // Host side of the 2-CTA tcgen05 GEMM (kernels in gemm_sm100.cuh, specialised
-// per operand layout and tile width in gemm_sm100_k256.cu / _k128.cu / _mn.cu) and the split-K
+// per operand layout and tile shape in gemm_sm100_k2.cu / _k2n.cu / _k1.cu / _mn.cu) and the split-K
 // reduction kernel.
 #include "gemm_sm100.cuh"
 
@@ -108,16 +108,18 @@ __device__ __forceinline__ void epi8(const Args& p, int64_t m, int n, const floa
 // One thread per 8 columns of one accumulator row: sums the `splits`
 // partials (split 0 first) from the workspace and runs the epilogue.
 __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restrict__ ws, const Args p) {
-  const int BN = p.bn, CH = BN / 8;
+  pdl_wait();  // launched as a programmatic dependent of the GEMM that wrote the partials
+  pdl_trigger();
+  const int BN = p.bn, CH = BN / 8, BMT = HM * p.cg;
   const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  const int64_t total = (int64_t)p.tiles * BM * CH;
+  const int64_t total = (int64_t)p.tiles * BMT * CH;
   if (idx >= total) return;
   const int ch = (int)(idx % CH);
-  const int row = (int)((idx / CH) % BM);  // 0..255 inside the tile (half = row / 128)
-  const int t = (int)(idx / ((int64_t)CH * BM));
+  const int row = (int)((idx / CH) % BMT);  // row inside the tile (CTA of the pair = row / 128)
+  const int t = (int)(idx / ((int64_t)CH * BMT));
   int mt, nt, split;
   tile_of(p, t * p.splits, mt, nt, split);
-  const int64_t m = (int64_t)mt * BM + row;
+  const int64_t m = (int64_t)mt * BMT + row;
   const int n = nt * BN + ch * 8;
   if (m >= p.M || n >= p.N) return;
   const int half = row / HM, r_in = row % HM;
@@ -125,7 +127,7 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restr
 #pragma unroll
   for (int i = 0; i < 8; ++i) acc[i] = 0.f;
   for (int s = 0; s < p.splits; ++s) {
-    const int64_t wrow = ((int64_t)(t * p.splits + s) * 2 + half) * HM + r_in;
+    const int64_t wrow = ((int64_t)(t * p.splits + s) * p.cg + half) * HM + r_in;
     float v[8];
     ld8f(ws + wrow * BN + ch * 8, v);
 #pragma unroll
@@ -170,11 +172,11 @@ CUtensorMap epi_map(const at::Tensor& t, uint64_t cols, uint64_t rows, uint32_t 
 }
 
 // Split-K count for `tiles` output tiles over a K of `kb` 64-wide slices on
-// `ncl` CTA pairs.  Cost in units of one 64-wide slice of a 256 x 256 tile:
+// `ncl` CTA pairs.  Cost in units of one 64-wide slice of a tile's MMAs:
 // waves x slices per split, plus, whenever partials are written (split-K, or
 // an epilogue that always goes through them), about 12 units per work item
-// for the fp32 partial (256 KB) and its share of the reduction.  At least 8
-// slices per split.
+// for the fp32 partial and its share of the reduction, and 20 units for the
+// reduction kernel's launch and ramp.  At least 8 slices per split.
 int choose_splits(int tiles, int kb, int ncl, bool partial_anyway) {
   int best = 1;
   double best_cost = 1e30;
@@ -185,7 +187,7 @@ int choose_splits(int tiles, int kb, int ncl, bool partial_anyway) {
     const int items = tiles * s;
     const int waves = (items + ncl - 1) / ncl;
     double cost = (double)waves * per;
-    if (s > 1 || partial_anyway) cost += 12.0 * waves + 12.0 * items / ncl;
+    if (s > 1 || partial_anyway) cost += 12.0 * waves + 12.0 * items / ncl + 20.0;
     if (cost < best_cost - 1e-9) {
       best_cost = cost;
       best = s;
@@ -273,24 +275,39 @@ void gemm_sm100(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn, 
   a.M = (int)M;
   a.N = (int)N;
   a.K = (int)K;
-  a.n_mt = (int)((M + BM - 1) / BM);
+
   a.kb_total = (int)((K + BK - 1) / BK);
   const int ncl = std::max(1, num_sms() / 2);
-  // 256 x 256 tiles, or 256 x 128 when the 256-wide tiles would leave CTA
-  // pairs idle in a single partial wave and halving them fills more of the GPU
-  // (weight gradients, both operands MN-major, fill the GPU with split-K instead)
-  const auto n_tiles = [&](int bn) {
-    return a.n_mt * (swiglu ? (int)((ffn_f + bn / 2 - 1) / (bn / 2)) : (int)((N + bn - 1) / bn));
+  const bool state_f32_req = mode == MEM_UPDATE && Cout.scalar_type() == at::kFloat;
+  // Tile shape: 256 x 256 on CTA pairs; 256 x 128 on CTA pairs when the
+  // 256-wide tiles would not fill one wave of pairs (weight gradients fill
+  // the GPU with split-K instead); 128 x 128 on single CTAs for at most 128
+  // rows (a pair's second half would be empty).  A single CTA streaming
+  // 128 x 128 x 64 per stage is bound by shared-memory bandwidth at about
+  // half the tensor rate, so it is not used where pairs fit.
+  const auto n_tiles = [&](int bm, int bn) {
+    return (int)((M + bm - 1) / bm) *
+           (swiglu ? (int)((ffn_f + bn / 2 - 1) / (bn / 2)) : (int)((N + bn - 1) / bn));
   };
-  int BN = 256;
-  if (!(a_mn && b_mn) && n_tiles(256) < ncl && n_tiles(128) > n_tiles(256)) BN = 128;
+  int BN = 256, CG = 2;
+  if (M <= HM) {
+    BN = 128;
+    CG = 1;
+  } else if (!(a_mn && b_mn) && n_tiles(256, 256) < ncl && n_tiles(256, 128) > n_tiles(256, 256)) {
+    BN = 128;
+  }
   a.bn = BN;
+  a.cg = CG;
+  a.n_mt = (int)((M + HM * CG - 1) / (HM * CG));
   a.n_nt = swiglu ? (int)((ffn_f + BN / 2 - 1) / (BN / 2)) : (int)((N + BN - 1) / BN);
   a.tiles = a.n_mt * a.n_nt;
+  const int ngroups = std::max(1, num_sms() / CG);  // tile groups that run at once
   const bool split_ok = !swiglu;
   int s = (int)splits;
-  const bool partial_anyway = !(mode == STORE || mode == RESID || mode == ACT || mode == ERR || mode == ACT_GRAD);
-  if (s <= 0) s = split_ok ? choose_splits(a.tiles, a.kb_total, ncl, partial_anyway) : 1;
+  const bool partial_anyway =
+      !(mode == STORE || mode == RESID || mode == ACT || mode == ERR || mode == ACT_GRAD || mode == SWIGLU ||
+        mode == SWIGLU_BWD || (a_mn && b_mn && (mode == ACCUM || (mode == MEM_UPDATE && !state_f32_req))));
+  if (s <= 0) s = split_ok ? choose_splits(a.tiles, a.kb_total, ngroups, partial_anyway) : 1;
   TORCH_CHECK(s == 1 || split_ok, "gemm_sm100: this epilogue does not take split-K");
   s = std::max(1, std::min(s, a.kb_total));
   a.kb_per_split = (a.kb_total + s - 1) / s;
@@ -338,6 +355,8 @@ void gemm_sm100(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn, 
       kmode = (int)mode;
     else if (!a_mn && b_mn && (mode == STORE || (mode == ACT_GRAD && silu) || mode == SWIGLU_BWD))
       kmode = (int)mode;
+    else if (a_mn && b_mn && (mode == ACCUM || (mode == MEM_UPDATE && !a.state_f32)))
+      kmode = (int)mode;
     else if (mode == STORE)
       kmode = STORE;
   }
@@ -347,8 +366,9 @@ void gemm_sm100(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn, 
   const uint32_t bc = kmode == SWIGLU ? 32 : 64;
   mp.c = epi_map(Cout, c_cols, M, bc);
   mp.c2 = C2.has_value() ? epi_map(*C2, c2_cols, M, bc) : mp.c;
-  mp.r = (needs_r && mode != MEM_UPDATE) ? epi_map(*R, N, M, bc) : mp.c;
-  mp.r2 = mp.c;
+  mp.r = needs_r ? epi_map(*R, N, M, bc) : mp.c;
+  if (mode == ACCUM) mp.r = mp.c;
+  mp.r2 = (mode == MEM_UPDATE && !a.state_f32) ? epi_map(*R2, N, M, bc) : mp.c;
   if (mode == SWIGLU_BWD) {  // [dg | du] and [g | u] as two F-column halves each
     mp.c = epi_map(Cout, N, M, bc);
     mp.c2 = epi_map(Cout.narrow(1, N, N), N, M, bc);
@@ -357,28 +377,39 @@ void gemm_sm100(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn, 
   mp.ws = mp.c;
   at::Tensor ws;
   if (kmode == PARTIAL) {
-    // fp32 partial tile-halves [items * 256, BN]
-    ws = at::empty({(int64_t)a.items * 2 * HM, BN}, A.options().dtype(at::kFloat));
-    mp.ws = epi_map(ws, BN, (uint64_t)a.items * 2 * HM);
+    // fp32 partials, 128 rows per CTA of each work item: [items * CG * 128, BN]
+    ws = at::empty({(int64_t)a.items * CG * HM, BN}, A.options().dtype(at::kFloat));
+    mp.ws = epi_map(ws, BN, (uint64_t)a.items * CG * HM);
   }
   cudaStream_t st = stream();
 #define TB_G2(AM, BMN, MD)                                                          \
   if (a_mn == AM && b_mn == BMN && kmode == MD) {                                     \
-    if (BN == 256) launch_gemm2<AM, BMN, MD, 256>(mp, a, st);                         \
-    else launch_gemm2<AM, BMN, MD, 128>(mp, a, st);                                   \
+    if (CG == 1) launch_gemm2<AM, BMN, MD, 128, 1>(mp, a, st);                        \
+    else if (BN == 256) launch_gemm2<AM, BMN, MD, 256, 2>(mp, a, st);                 \
+    else launch_gemm2<AM, BMN, MD, 128, 2>(mp, a, st);                                \
     goto launched;                                                                    \
   }
   TB_G2(false, false, STORE) TB_G2(false, false, RESID) TB_G2(false, false, ACT) TB_G2(false, false, ERR)
   TB_G2(false, false, SWIGLU) TB_G2(false, false, PARTIAL)
   TB_G2(false, true, STORE) TB_G2(false, true, ACT_GRAD) TB_G2(false, true, SWIGLU_BWD) TB_G2(false, true, PARTIAL)
-  TB_G2(true, true, STORE) TB_G2(true, true, PARTIAL) TB_G2(true, false, STORE) TB_G2(true, false, PARTIAL)
+  TB_G2(true, true, STORE) TB_G2(true, true, ACCUM) TB_G2(true, true, MEM_UPDATE) TB_G2(true, true, PARTIAL)
+  TB_G2(true, false, STORE) TB_G2(true, false, PARTIAL)
 #undef TB_G2
   TORCH_CHECK(false, "gemm_sm100: no kernel for this layout / epilogue");
 launched:
   check_launch("gemm_sm100");
   if (kmode == PARTIAL) {
-    const int64_t total = (int64_t)a.tiles * BM * (BN / 8);
-    splitk_reduce_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(ws.data_ptr<float>(), a);
+    const int64_t total = (int64_t)a.tiles * HM * CG * (BN / 8);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)((total + 255) / 256));
+    cfg.blockDim = dim3(256);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, splitk_reduce_kernel, (const float*)ws.data_ptr<float>(), a));
     check_launch("gemm_sm100 split-K reduce");
   }
 }

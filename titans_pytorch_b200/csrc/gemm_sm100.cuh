@@ -99,6 +99,7 @@ struct Args {
   int b_nstep, b_rstep;  // B-half row origin = nt * b_nstep + rank * b_rstep
   int mode, act, ffn_f, state_f32;
   int bn;  // tile columns (the kernel's BN; read by the split-K reduction)
+  int cg;  // CTAs per tile (2: CTA pair, 256 rows; 1: one CTA, 128 rows)
   float scale;
   void* c;
   int64_t ldc;
@@ -122,10 +123,10 @@ struct Maps {
   CUtensorMap a, b, c, c2, r, r2, ws;
 };
 
-template <int BN>
+template <int BN, int CG>
 struct Cfg {
   static constexpr int A_BYTES = HM * BK * 2;
-  static constexpr int B_BYTES = (BN / 2) * BK * 2;
+  static constexpr int B_BYTES = (BN / CG) * BK * 2;  // this CTA's B rows
   static constexpr int STAGE = A_BYTES + B_BYTES;
   static constexpr int NS = (160 * 1024) / STAGE;
   static constexpr int OFF_STG = NS * STAGE;
@@ -139,6 +140,12 @@ __device__ __forceinline__ uint32_t cluster_rank() {
   asm volatile("mov.u32 %0, %%cluster_ctarank;\n" : "=r"(r));
   return r;
 }
+// Programmatic dependent launch: the kernel is launched so that it may start
+// while the previous kernel on the stream is still running; wait() blocks
+// until that kernel has completed and its writes are visible, trigger() lets
+// the next kernel start its own prologue early.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory"); }
 __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;\n" ::: "memory");
 }
@@ -196,6 +203,23 @@ __device__ __forceinline__ void tmem_relinquish2() {
 __device__ __forceinline__ void tmem_dealloc2(uint32_t taddr, uint32_t ncols) {
   asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;\n" ::"r"(taddr), "r"(ncols) : "memory");
 }
+// The CTA-group generic forms (CG = 2: CTA pair, CG = 1: one CTA); every
+// tcgen05 instruction of a kernel uses the same group.
+template <int CG>
+__device__ __forceinline__ void tmem_alloc_g(uint32_t* dst_smem, uint32_t ncols) {
+  if constexpr (CG == 2) tmem_alloc2(dst_smem, ncols);
+  else tc::tmem_alloc(dst_smem, ncols);
+}
+template <int CG>
+__device__ __forceinline__ void tmem_relinquish_g() {
+  if constexpr (CG == 2) tmem_relinquish2();
+  else tc::tmem_relinquish();
+}
+template <int CG>
+__device__ __forceinline__ void tmem_dealloc_g(uint32_t taddr, uint32_t ncols) {
+  if constexpr (CG == 2) tmem_dealloc2(taddr, ncols);
+  else tc::tmem_dealloc(taddr, ncols);
+}
 __device__ __forceinline__ void umma2_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
                                            uint32_t accumulate) {
   asm volatile(
@@ -214,6 +238,18 @@ __device__ __forceinline__ void umma2_commit_both(uint64_t* bar) {
       : "memory");
 }
 
+template <int CG>
+__device__ __forceinline__ void umma_g(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                       uint32_t accumulate) {
+  if constexpr (CG == 2) umma2_bf16(tmem_d, adesc, bdesc, idesc, accumulate);
+  else tc::umma_bf16(tmem_d, adesc, bdesc, idesc, accumulate);
+}
+template <int CG>
+__device__ __forceinline__ void commit_g(uint64_t* bar) {
+  if constexpr (CG == 2) umma2_commit_both(bar);
+  else tc::umma_commit(bar);
+}
+
 // ------------------------------------------------------------------ epilogue blocks
 // 2-D TMA load into this CTA's shared memory completing on a local barrier
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1) {
@@ -222,6 +258,20 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
           tc::smem_addr(dst)),
       "l"(map), "r"(c0), "r"(c1), "r"(tc::smem_addr(bar))
       : "memory");
+}
+// mainloop operand load: CG = 2 completes on the leader's barrier (cta_group::2
+// form, shared::cluster address), CG = 1 on this CTA's own barrier
+template <int CG>
+__device__ __forceinline__ void op_load(void* dst, const CUtensorMap* map, uint32_t bar_addr, int c0, int c1) {
+  if constexpr (CG == 2) {
+    tma_load_2d_pair(dst, map, bar_addr, c0, c1);
+  } else {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];\n" ::
+            "r"(tc::smem_addr(dst)),
+        "l"(map), "r"(c0), "r"(c1), "r"(bar_addr)
+        : "memory");
+  }
 }
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int c0, int c1) {
   asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];\n" ::"l"(map), "r"(c0),
@@ -370,13 +420,15 @@ constexpr int blk_bytes() {
 // bytes of input a MODE reads per step
 template <int MODE>
 constexpr uint32_t in_bytes() {
-  return (MODE == RESID || MODE == ACT_GRAD || MODE == ERR) ? (uint32_t)blk_bytes<MODE>()
-                                                            : (MODE == SWIGLU_BWD ? 2u * blk_bytes<MODE>() : 0u);
+  return (MODE == RESID || MODE == ACCUM || MODE == ACT_GRAD || MODE == ERR)
+             ? (uint32_t)blk_bytes<MODE>()
+             : ((MODE == SWIGLU_BWD || MODE == MEM_UPDATE) ? 2u * blk_bytes<MODE>() : 0u);
 }
 // staging of one step (its input and output blocks)
 template <int MODE>
 constexpr int slot_bytes() {
-  return MODE == SWIGLU ? 3 * blk_bytes<MODE>() : ((MODE == ACT || MODE == SWIGLU_BWD) ? 2 : 1) * blk_bytes<MODE>();
+  return MODE == SWIGLU ? 3 * blk_bytes<MODE>()
+                       : ((MODE == ACT || MODE == SWIGLU_BWD || MODE == MEM_UPDATE) ? 2 : 1) * blk_bytes<MODE>();
 }
 
 // lane 0: loads the inputs of the block at output column n (rows row0..+31)
@@ -385,7 +437,7 @@ __device__ __forceinline__ void issue_in(const Maps& mp, int ffn_f, uint8_t* sb,
   if constexpr (in_bytes<MODE>() > 0) {
     tc::mbar_expect_tx(bar, in_bytes<MODE>());
     tma_load_2d(sb, &mp.r, bar, n, row0);
-    if constexpr (MODE == SWIGLU_BWD) tma_load_2d(sb + blk_bytes<MODE>(), &mp.r2, bar, n, row0);
+    if constexpr (MODE == SWIGLU_BWD || MODE == MEM_UPDATE) tma_load_2d(sb + blk_bytes<MODE>(), &mp.r2, bar, n, row0);
   }
 }
 
@@ -420,10 +472,11 @@ __device__ __forceinline__ void ld_row128(const uint8_t* blk, int r, uint32_t (&
   }
 }
 
-template <bool A_MN, bool B_MN, int MODE, int BN>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
+template <bool A_MN, bool B_MN, int MODE, int BN, int CG>
+__global__ void __cluster_dims__(CG, 1, 1) __launch_bounds__(NTHREADS, 1)
     gemm2_kernel(const __grid_constant__ Maps mp, const Args p) {
-  using C = Cfg<BN>;
+  using C = Cfg<BN, CG>;
+  constexpr int BMT = HM * CG;  // tile rows
   constexpr int NS = C::NS;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -436,8 +489,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint32_t rank = cluster_rank();
-  const int cid = blockIdx.x >> 1, ncl = gridDim.x >> 1;
+  const uint32_t rank = CG == 2 ? cluster_rank() : 0u;
+  const int cid = blockIdx.x / CG, ncl = gridDim.x / CG;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < NS; ++s) {
@@ -446,58 +499,70 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
     }
     for (int b = 0; b < 2; ++b) {
       tc::mbar_init(bar_acc_full + b, 1);
-      tc::mbar_init(bar_acc_empty + b, 2 * 4);  // one arrival per epilogue warp of both CTAs
+      tc::mbar_init(bar_acc_empty + b, CG * 4);  // one arrival per epilogue warp of every CTA of the tile
     }
     for (int b = 0; b < 32; ++b) tc::mbar_init(bar_ld + b, 1);
     *abort_flag = 0;
     tc::mbar_fence_init();
   }
   if (warp == 1) {
-    tmem_alloc2(tmem_slot, TM_COLS);
-    tmem_relinquish2();
+    tmem_alloc_g<CG>(tmem_slot, TM_COLS);
+    tmem_relinquish_g<CG>();
   }
   tc::tc_fence_before();
   __syncthreads();
   cluster_sync();  // barriers of both CTAs initialised before any remote arrive / complete_tx
   tc::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // Everything above touched only this CTA's shared and tensor memory, so it
+  // overlapped the previous kernel; global memory is read and written below.
+  pdl_wait();
+  pdl_trigger();
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer (both CTAs)
     if (lane == 0) {
       tc::tma_prefetch_desc(&mp.a);
       tc::tma_prefetch_desc(&mp.b);
-      const uint32_t full0 = mapa(tc::smem_addr(bar_full), 0);  // the leader's full barriers
+      // the leader's full barriers (a single CTA's own)
+      const uint32_t full0 = CG == 2 ? mapa(tc::smem_addr(bar_full), 0) : tc::smem_addr(bar_full);
       int it = 0;
       bool ok = true;
       for (int item = cid; ok && item < p.items; item += ncl) {
         int mt, nt, split;
         tile_of(p, item, mt, nt, split);
         const int kb0 = split * p.kb_per_split, kb1 = min(p.kb_total, kb0 + p.kb_per_split);
-        const int m0 = mt * BM + (int)rank * HM;
-        const int n0 = nt * p.b_nstep + (int)rank * p.b_rstep;
+        const int m0 = mt * BMT + (int)rank * HM;
         for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % NS;
           if (it >= NS && !tc::mbar_wait(bar_empty + s, ((it / NS) - 1) & 1, abort_flag, p.err)) {
             ok = false;
             break;
           }
-          if (rank == 0) tc::mbar_expect_tx(bar_full + s, 2 * C::STAGE);
+          if (rank == 0) tc::mbar_expect_tx(bar_full + s, CG * C::STAGE);
           uint8_t* sa = smem + s * C::STAGE;
           uint8_t* sbm = sa + C::A_BYTES;
           const uint32_t fb = full0 + s * 8;
           const int k0 = kb * BK;
           if constexpr (A_MN) {
 #pragma unroll
-            for (int j = 0; j < HM / 64; ++j) tma_load_2d_pair(sa + j * 8192, &mp.a, fb, m0 + 64 * j, k0);
+            for (int j = 0; j < HM / 64; ++j) op_load<CG>(sa + j * 8192, &mp.a, fb, m0 + 64 * j, k0);
           } else {
-            tma_load_2d_pair(sa, &mp.a, fb, k0, m0);
+            op_load<CG>(sa, &mp.a, fb, k0, m0);
           }
-          if constexpr (B_MN) {
+          // B: the tile's two halves of BN / 2 rows (gate / up rows for the SwiGLU);
+          // a CTA of a pair loads its own half, a single CTA both
 #pragma unroll
-            for (int j = 0; j < BN / 128; ++j) tma_load_2d_pair(sbm + j * 8192, &mp.b, fb, n0 + 64 * j, k0);
-          } else {
-            tma_load_2d_pair(sbm, &mp.b, fb, k0, n0);
+          for (int hh = 0; hh < 2 / CG; ++hh) {
+            const int half = CG == 2 ? (int)rank : hh;
+            const int n0 = nt * p.b_nstep + half * p.b_rstep;
+            if constexpr (B_MN) {
+#pragma unroll
+              for (int j = 0; j < BN / 128; ++j)
+                op_load<CG>(sbm + hh * (BN / 128) * 8192 + j * 8192, &mp.b, fb, n0 + 64 * j, k0);
+            } else {
+              op_load<CG>(sbm + hh * (BN / 2) * 128, &mp.b, fb, k0, n0);
+            }
           }
         }
       }
@@ -510,7 +575,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer (leader)
     if (rank == 0 && lane == 0) {
-      constexpr uint32_t idesc = tc::idesc_bf16_f32(BM, BN, A_MN, B_MN);
+      constexpr uint32_t idesc = tc::idesc_bf16_f32(BMT, BN, A_MN, B_MN);
       int it = 0, li = 0;
       bool ok = true;
       for (int item = cid; ok && item < p.items; item += ncl, ++li) {
@@ -518,7 +583,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
         tile_of(p, item, mt, nt, split);
         const int kb0 = split * p.kb_per_split, kb1 = min(p.kb_total, kb0 + p.kb_per_split);
         const int buf = li & 1;
-        if (li >= 2 && !mbar_wait_cluster(bar_acc_empty + buf, ((li >> 1) - 1) & 1, abort_flag, p.err)) break;
+        if (li >= 2 && !(CG == 2 ? mbar_wait_cluster(bar_acc_empty + buf, ((li >> 1) - 1) & 1, abort_flag, p.err)
+                                  : tc::mbar_wait(bar_acc_empty + buf, ((li >> 1) - 1) & 1, abort_flag, p.err)))
+          break;
         tc::tc_fence_after();
         const uint32_t d = tmem + buf * BN;
         for (int kb = kb0; kb < kb1; ++kb, ++it) {
@@ -533,11 +600,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
           for (int k = 0; k < BK / 16; ++k) {
             const uint64_t ad = A_MN ? tc::sdesc_sw128(aA + k * 2048, 8192, 1024) : tc::sdesc_sw128(aA + 32 * k, 16, 1024);
             const uint64_t bd = B_MN ? tc::sdesc_sw128(aB + k * 2048, 8192, 1024) : tc::sdesc_sw128(aB + 32 * k, 16, 1024);
-            umma2_bf16(d, ad, bd, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
+            umma_g<CG>(d, ad, bd, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
           }
-          umma2_commit_both(bar_empty + s);
+          commit_g<CG>(bar_empty + s);
         }
-        if (ok) umma2_commit_both(bar_acc_full + buf);
+        if (ok) commit_g<CG>(bar_acc_full + buf);
       }
     }
   } else {
@@ -553,7 +620,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
     uint8_t* stg = smem + C::OFF_STG + e * STG_WARP;
     uint64_t* bl = bar_ld + 8 * e;
     uint32_t phase = 0;  // bit s: phase of slot s's load barrier
-    const uint32_t acc_empty0 = mapa(tc::smem_addr(bar_acc_empty), 0);
+    const uint32_t acc_empty0 = CG == 2 ? mapa(tc::smem_addr(bar_acc_empty), 0) : tc::smem_addr(bar_acc_empty);
     const float scale = p.scale;
     const int ffn_f = p.ffn_f;
     // prefetch cursor (inputs only): next (item, step) whose inputs are requested
@@ -562,7 +629,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
       while (pf_k < upto && pf_item < p.items) {
         int pmt, pnt, psp;
         tile_of(p, pf_item, pmt, pnt, psp);
-        const int prow0 = pmt * BM + (int)rank * HM + q * 32;
+        const int prow0 = pmt * BMT + (int)rank * HM + q * 32;
         const int slot = pf_k % NSLOT;
         issue_in<MODE>(mp, ffn_f, stg + slot * SLOT, step_col<MODE, BN>(pnt, pf_c), prow0, bl + slot);
         ++pf_k;
@@ -581,12 +648,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
       int mt, nt, split;
       tile_of(p, item, mt, nt, split);
       const int buf = li & 1;
-      const int row0 = mt * BM + (int)rank * HM + q * 32;
+      const int row0 = mt * BMT + (int)rank * HM + q * 32;
       const int nsteps = step_count<MODE, BN>(p, nt);
       if (!tc::mbar_wait(bar_acc_full + buf, (li >> 1) & 1, abort_flag, p.err)) break;
       tc::tc_fence_after();
       const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + buf * BN;
-      const int wrow = (item * 2 + (int)rank) * HM + q * 32;  // PARTIAL: workspace rows
+      const int wrow = (item * CG + (int)rank) * HM + q * 32;  // PARTIAL: workspace rows
       for (int c = 0; c < nsteps; ++c, ++step) {
         const int slot = step % NSLOT;
         uint8_t* sb = stg + slot * SLOT;
@@ -642,10 +709,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
           if constexpr (MODE == STORE) {
 #pragma unroll
             for (int i = 0; i < 32; ++i) w[i] = pack2(v[2 * i], v[2 * i + 1]);
-          } else if constexpr (MODE == RESID) {
+          } else if constexpr (MODE == RESID || MODE == ACCUM) {
             ld_row128(sb, lane, w);
 #pragma unroll
             for (int i = 0; i < 32; ++i) w[i] = pack2(lo_bf(w[i]) + v[2 * i], hi_bf(w[i]) + v[2 * i + 1]);
+          } else if constexpr (MODE == MEM_UPDATE) {
+            // bf16 state: S' = bf16(eta S - theta G); W' = (1 - alpha) W + S'
+            uint32_t sw[32];
+            ld_row128(sb, lane, w);
+            ld_row128(sb + BB, lane, sw);
+            const float alpha = p.gates[0], theta = p.gates[1], eta = p.gates[2];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              sw[i] = pack2(eta * lo_bf(sw[i]) - theta * v[2 * i], eta * hi_bf(sw[i]) - theta * v[2 * i + 1]);
+              w[i] = pack2((1.f - alpha) * lo_bf(w[i]) + lo_bf(sw[i]), (1.f - alpha) * hi_bf(w[i]) + hi_bf(sw[i]));
+            }
+            st_row128(sb + BB, lane, sw);
           } else if constexpr (MODE == ERR) {
             ld_row128(sb, lane, w);
 #pragma unroll
@@ -694,7 +773,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
             tma_store_2d(&mp.c2, sb, n, row0);
             tma_store_2d(&mp.c2, sb + BB, ffn_f + n, row0);
             tma_store_2d(&mp.c, sb + 2 * BB, n, row0);
-          } else if constexpr (MODE == SWIGLU_BWD) {
+          } else if constexpr (MODE == SWIGLU_BWD || MODE == MEM_UPDATE) {
             tma_store_2d(&mp.c, sb, n, row0);
             tma_store_2d(&mp.c2, sb + BB, n, row0);
           } else if constexpr (MODE == ACT) {
@@ -730,34 +809,44 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
   __syncthreads();
   cluster_sync();  // the peer's MMAs / remote arrivals are done before TMEM and shared memory go away
   tc::tc_fence_after();
-  if (warp == 1) tmem_dealloc2(tmem, TM_COLS);
+  if (warp == 1) tmem_dealloc_g<CG>(tmem, TM_COLS);
 }
 
 // Launch of one specialisation (defined in the per-layout translation units).
-template <bool A_MN, bool B_MN, int MODE, int BN>
+template <bool A_MN, bool B_MN, int MODE, int BN, int CG>
 void launch_gemm2(const Maps& mp, const Args& a, cudaStream_t st);
 
-// Grid: one CTA pair per co-resident cluster slot (at most SMs / 2), at most one per work item.
-template <bool A_MN, bool B_MN, int MODE, int BN>
+// Grid: one tile group (CTA pair or CTA) per co-resident cluster slot, at most one per work item.
+template <bool A_MN, bool B_MN, int MODE, int BN, int CG>
 void launch_gemm2_impl(const Maps& mp, const Args& a, cudaStream_t st) {
   static int ncl_max = -1;
-  using C = Cfg<BN>;
-  auto kern = gemm2_kernel<A_MN, B_MN, MODE, BN>;
+  using C = Cfg<BN, CG>;
+  auto kern = gemm2_kernel<A_MN, B_MN, MODE, BN, CG>;
   if (ncl_max < 0) {
     C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(2 * (num_sms() / 2));
+    cfg.gridDim = dim3(CG * (num_sms() / CG));
     cfg.blockDim = dim3(NTHREADS);
     cfg.dynamicSmemBytes = C::SMEM;
     int c = 0;
     if (cudaOccupancyMaxActiveClusters(&c, kern, &cfg) != cudaSuccess || c <= 0) {
       cudaGetLastError();
-      c = num_sms() / 2;
+      c = num_sms() / CG;
     }
-    ncl_max = std::min(c, num_sms() / 2);
+    ncl_max = std::min(c, num_sms() / CG);
   }
   const int ncl = std::min(a.items, ncl_max);
-  kern<<<2 * ncl, NTHREADS, C::SMEM, st>>>(mp, a);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(CG * ncl);
+  cfg.blockDim = dim3(NTHREADS);
+  cfg.dynamicSmemBytes = C::SMEM;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, mp, a));
 }
 
 }  // namespace g2

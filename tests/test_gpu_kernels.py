@@ -150,10 +150,14 @@ def test_window_attention(case):
         assert rel_err(pkv.grad, pr.grad) < 2e-2
 
 
+@pytest.mark.parametrize("shape", [(2, 50, 64, 128), (1, 37, 64, 256), (3, 333, 96, 384)])
 @pytest.mark.parametrize("L_M,linear_silu", [(1, True), (1, False), (2, False), (3, False)])
-def test_memory_step(L_M, linear_silu):
+def test_memory_step(L_M, linear_silu, shape):
+    """Fused tcgen05 memory update (act / error / act' epilogues, gated update in
+    the weight-gradient epilogue) vs the fp32 reference-semantics update
+    (``memory_grads_reference``), odd token counts included."""
     torch.manual_seed(5)
-    B, T, D, Hm = 2, 50, 64, 128
+    B, T, D, Hm = shape
     dtype = torch.bfloat16
     k = F.normalize(torch.randn(B, T, D, device=DEV), dim=-1).to(dtype)
     v = torch.randn(B, T, D, device=DEV).to(dtype)
@@ -232,16 +236,30 @@ def test_attention_tcgen05_forward(case, d):
     assert float((l_tc - lse_ref).abs().max()) < 2e-2
 
 
-# the last two: several work items per persistent CTA (B*H*items > SM count),
+def dense_attention_grads(Q, K, V, dO, P, W, scale):
+    """fp32 autograd through a dense-mask attention: (dQ, dK, dV) in [B, H, *, d]."""
+    from titans_pytorch_b200.ops.attention import prefix_window_mask
+    T = Q.shape[2]
+    q, k, v = (x.float().requires_grad_() for x in (Q, K, V))
+    s = torch.einsum("bhid,bhjd->bhij", q, k) * scale
+    s = s.masked_fill(~prefix_window_mask(T, P, W, DEV), float("-inf"))
+    o = torch.einsum("bhij,bhjd->bhid", torch.softmax(s, -1), v)
+    o.backward(dO.float().transpose(1, 2))
+    return q.grad, k.grad, v.grad
+
+
+# the last four: several work items per persistent CTA (B*H*items > SM count),
 # with no-window tiles split over several items
+@pytest.mark.parametrize("d", [64, 96])
 @pytest.mark.parametrize("case", TC_CASES + [(1, 2, 1100, 4, 512), (2, 1, 700, 16, 100), (4, 8, 1024, 4, 256),
                                              (2, 4, 2048, 8, 1 << 30)])
-def test_attention_tcgen05_backward(case):
-    """tcgen05 backward vs the mma.sync backward (both against the same forward outputs)."""
+def test_attention_tcgen05_backward(case, d):
+    """tcgen05 backward (head dim 64: one fused kernel; 96: dK/dV key-major +
+    dQ query-major kernels) vs fp32 autograd through a dense-mask attention,
+    and vs the mma.sync backward (all from the same forward outputs)."""
     B, H, T, P, W = case
     E = _ext.ext()
     torch.manual_seed(8)
-    d = 64
     Q = torch.randn(B, H, T, d, device=DEV, dtype=torch.bfloat16)
     K = torch.randn(B, H, P + T, d, device=DEV, dtype=torch.bfloat16)
     V = torch.randn(B, H, P + T, d, device=DEV, dtype=torch.bfloat16)
@@ -252,8 +270,11 @@ def test_attention_tcgen05_backward(case):
     r = E.attn_bwd_packed(dO, Q, K, V, O, lse, W, scale)
     torch.cuda.synchronize()
     assert E.kernel_error_status(0, True) == 0
-    for x, y in zip(a, r):
-        assert rel_err(x, y) < 1e-2
+    ref = dense_attention_grads(Q, K, V, dO, P, W, scale)
+    for x, y, z in zip(a, r, ref):
+        assert x.shape == z.shape
+        assert rel_err(x, z) < 2e-2
+        assert rel_err(x, y) < 1.5e-2
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])

@@ -23,7 +23,7 @@ max over ranks is reported.  Roofline of the fused step, per rank:
   written (24 B) and the local bf16 weights written (2 B); per element of the
   other ranks' shards, their loads of this GPU's gradient (2 B) and their
   stores of the new weights into this GPU's buffer (2 B); at the measured
-  6537 GB/s copy rate.
+  copy rate (``hbm_gbs`` of ``MEASURED_PEAKS.json``).
 
 The fused step's fraction is the slower of the two roofline times divided by
 the measured time.
@@ -147,14 +147,19 @@ def main(argv=None) -> None:
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--steps", type=int, default=10)
     p.add_argument("--link-gbs", type=float, default=770.0)
-    p.add_argument("--hbm-gbs", type=float, default=6537.3)
+    p.add_argument("--hbm-gbs", type=float, default=None, help="default: the measured copy rate")
     p.add_argument("--what", choices=["dp_step", "gather_gemm", "all"], default="all")
     p.add_argument("--gemm-m", type=int, default=8 * 4096)
     p.add_argument("--gemm-n", type=int, default=3 * 768)
     p.add_argument("--gemm-k", type=int, default=768)
     p.add_argument("--unit-params", type=float, default=18.284544, help="millions of parameters gathered")
-    p.add_argument("--gemm-tflops", type=float, default=1670.1, help="measured bf16 GEMM burst peak")
+    p.add_argument("--gemm-tflops", type=float, default=None, help="default: the measured bf16 GEMM burst peak")
     a = p.parse_args(argv)
+    from ..utils.perf import measured_peaks
+
+    peaks = measured_peaks()
+    a.hbm_gbs = peaks["hbm_gbs"] if a.hbm_gbs is None else a.hbm_gbs
+    a.gemm_tflops = peaks["bf16_tflops"] if a.gemm_tflops is None else a.gemm_tflops
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))

@@ -31,12 +31,9 @@ import torch
 
 
 def peak_tflops() -> float:
-    root = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
-    try:
-        with open(os.path.join(root, "MEASURED_PEAKS.json")) as f:
-            return float(json.load(f)["bf16_tflops"])
-    except (OSError, KeyError, ValueError):
-        return 1590.0
+    from ..utils.perf import measured_peaks
+
+    return measured_peaks()["bf16_tflops"]
 
 
 def timeit(fn, warmup: int, iters: int, flush: torch.Tensor) -> float:

@@ -8,7 +8,8 @@ untimed launches; an L2 flush (a write of a buffer larger than the 126 MB L2)
 runs between timed launches and is not inside the events.  One JSON line per
 op: median milliseconds, achieved TFLOP/s (contractions) or GB/s (memory-bound
 ops, algorithmic bytes), and the fraction of the given peaks.  The peak
-defaults are a bf16 cuBLAS GEMM burst and a device copy measured on B200.
+defaults are the measured bf16 cuBLAS GEMM burst and device copy rate
+(``MEASURED_PEAKS.json`` at the repository root).
 
 Shapes default to the training benchmark's (dim 768, 12 heads of 64, sequence
 4096, window 512, 4 persistent tokens); ``--batch`` is per launch.
@@ -134,9 +135,16 @@ def main(argv=None) -> None:
     add("--warmup", type=int, default=3)
     add("--iters", type=int, default=10)
     add("--no-flush", action="store_true")
-    add("--peak-tflops", type=float, default=1670.1, help="bf16 GEMM burst peak (measured cuBLAS on B200)")
-    add("--peak-gbs", type=float, default=6537.3, help="HBM copy peak (measured on B200)")
+    add("--peak-tflops", type=float, default=None, help="bf16 GEMM burst peak (default: the measured one)")
+    add("--peak-gbs", type=float, default=None, help="HBM copy peak (default: the measured one)")
     a = p.parse_args(argv)
+    from ..utils.perf import measured_peaks
+
+    peaks = measured_peaks()
+    if a.peak_tflops is None:
+        a.peak_tflops = peaks["bf16_tflops"]
+    if getattr(a, "peak_gbs", 0) is None:
+        a.peak_gbs = peaks["hbm_gbs"]
     flush = None if a.no_flush else torch.empty(64 << 20, device="cuda", dtype=torch.float32)
     for op in (OPS if a.op == "all" else (a.op,)):
         fn, flops, nbytes = build(op, a)

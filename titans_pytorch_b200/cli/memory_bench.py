@@ -60,8 +60,15 @@ def main(argv=None) -> None:
     add("--chunk", type=int, default=64)
     add("--warmup", type=int, default=1)
     add("--steps", type=int, default=3)
-    add("--peak-tflops", type=float, default=1670.1, help="bf16 GEMM burst peak (measured cuBLAS on B200)")
+    add("--peak-tflops", type=float, default=None, help="bf16 GEMM burst peak (default: the measured one)")
     a = p.parse_args(argv)
+    from ..utils.perf import measured_peaks
+
+    peaks = measured_peaks()
+    if a.peak_tflops is None:
+        a.peak_tflops = peaks["bf16_tflops"]
+    if getattr(a, "peak_gbs", 0) is None:
+        a.peak_gbs = peaks["hbm_gbs"]
     from ..ops.memory_paper import memory_scan
 
     dev = torch.device("cuda")

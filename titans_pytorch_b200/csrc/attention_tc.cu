@@ -542,7 +542,7 @@ int64_t kernel_error_status(int64_t device, bool reset) {
   return v;
 }
 
-bool attn_tc_supported(int64_t head_dim) { return head_dim == 64; }             // backward
+bool attn_tc_supported(int64_t head_dim) { return head_dim == 64 || head_dim == 96; }  // backward
 bool attn_tc_fwd_supported(int64_t head_dim) { return head_dim == 64 || head_dim == 96; }
 
 // Same contract as attn_fwd_packed: Q [B,H,T,64], K/V [B,H,P+T,64] bf16 contiguous
@@ -1091,11 +1091,17 @@ const at::Tensor& work_items(const at::Device& dev, int Tn, int P, int W) {
 
 }  // namespace attn_tcb
 
-// Same contract as attn_bwd_packed (head_dim 64): returns {dQa, dKa, dVa} fp32.
+std::vector<at::Tensor> attn_bwd_tc96(const at::Tensor& dO_in, const at::Tensor& Q, const at::Tensor& K,
+                                      const at::Tensor& V, const at::Tensor& O, const at::Tensor& LSE, int64_t window,
+                                      double scale);
+
+// Same contract as attn_bwd_packed (head_dim 64; head_dim 96 goes to
+// attn_bwd_tc96): returns {dQa, dKa, dVa} fp32.
 std::vector<at::Tensor> attn_bwd_tc(const at::Tensor& dO_in, const at::Tensor& Q, const at::Tensor& K,
                                     const at::Tensor& V, const at::Tensor& O, const at::Tensor& LSE, int64_t window,
                                     double scale) {
   using namespace attn_tcb;
+  if (Q.size(3) == 96) return attn_bwd_tc96(dO_in, Q, K, V, O, LSE, window, scale);
   const at::cuda::CUDAGuard g(Q.device());
   const int B = Q.size(0), H = Q.size(1), Tn = Q.size(2), hd = Q.size(3);
   TORCH_CHECK(hd == HD, "attn_bwd_tc: head_dim must be 64");

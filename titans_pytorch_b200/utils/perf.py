@@ -346,3 +346,23 @@ def speculative_decode(model, draft_model, input_ids: torch.Tensor, num_speculat
         m = int(agree.int().cumprod(0).sum())
         out = torch.cat([out, proposed[:, :m], choice[:, m:m + 1]], 1)
     return out[:, :input_ids.shape[1] + max_new_tokens]
+
+
+def measured_peaks() -> dict:
+    """Roofline denominators measured on the target B200s: ``MEASURED_PEAKS.json``
+    at the repository root (``hbm_gbs`` copy rate, ``bf16_tflops`` cuBLAS burst,
+    ``bf16_tflops_sustained``), else the earlier measurement on the same parts
+    (6650 GB/s, 1590 / 1400 TFLOP/s).  ``source`` says which."""
+    import json
+    import os
+
+    root = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    out = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+    try:
+        with open(os.path.join(root, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        out.update({k: float(d[k]) for k in ("hbm_gbs", "bf16_tflops", "bf16_tflops_sustained") if k in d})
+        out["source"] = "measured"
+    except (OSError, ValueError):
+        pass
+    return out

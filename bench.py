@@ -206,7 +206,7 @@ def count_launches(step_fn, prefixes) -> tuple[int, int]:
 
 
 # ---------------------------------------------------------------------------- arms
-def build_ours(device, world, parallel="dp"):
+def build_ours(device, world, parallel="dp", overlap=True, reshard=True):
     from titans_pytorch_b200 import TitansConfig, create_model
     from titans_pytorch_b200.train.trainer import Trainer, TrainStepConfig
     from titans_pytorch_b200.utils.perf import enable_gradient_checkpointing
@@ -219,11 +219,11 @@ def build_ours(device, world, parallel="dp"):
     if world > 1 and parallel == "fsdp":
         from titans_pytorch_b200.parallel.fsdp import FullyShardedEngine
 
-        engine = FullyShardedEngine()
+        engine = FullyShardedEngine(reshard=reshard, overlap=overlap)
     elif world > 1:
         from titans_pytorch_b200.parallel.ddp import DataParallelEngine
 
-        engine = DataParallelEngine()
+        engine = DataParallelEngine(overlap=overlap)
     # the whole step (with the fused data-parallel reduce/update for N > 1) is
     # captured in a CUDA graph: two eager warm-up steps, the capture on the third
     # warm-up call, replays in the timed region
@@ -317,6 +317,13 @@ def main():
     ap.add_argument("--parallel", choices=["dp", "fsdp"], default="dp",
                     help="N > 1, this framework: dp = replicated weights, optimizer state sharded; fsdp = "
                          "parameters sharded per block, all-gathered inside the first GEMM of the previous block")
+    ap.add_argument("--no-overlap", action="store_true",
+                    help="N > 1, this framework: reduce the gradients after the backward instead of per block "
+                         "during it")
+    ap.add_argument("--fsdp-mode", choices=["full", "grad-op"], default="full",
+                    help="fsdp: full = FULL_SHARD (parameters gathered per use into working slots, gradients "
+                         "reduce-scattered per block during the backward); grad-op = SHARD_GRAD_OP (gathered "
+                         "parameters kept until the step)")
     args = ap.parse_args()
     global CFG, MODEL_FIELDS, SEQ, MICRO_BATCH
     CFG = CONFIGS[args.config]
@@ -339,7 +346,8 @@ def main():
         trainer, nparams = built
         prefixes = ()
     else:
-        trainer, nparams = build_ours(device, world, args.parallel)
+        trainer, nparams = build_ours(device, world, args.parallel, overlap=not args.no_overlap,
+                                      reshard=args.fsdp_mode == "full")
         prefixes = ("tb::",)
 
     batches = make_batches(world, rank, W + K + 1)
@@ -395,12 +403,18 @@ def main():
     tokens = world * MICRO_BATCH * SEQ
     value = tokens / (ms / 1000)
     parallelism = f"dp{world}"
+    when = "after the backward" if args.no_overlap else "per block during the backward"
     if world > 1:
         parallelism = (f"dp{world} (grads all-reduced after backward)" if args.impl == "reference"
-                       else f"fsdp{world} (per-block parameter shards; all-gather fused into the previous "
-                            f"block's first tcgen05 GEMM; fused reduce-scatter / AdamW shard)"
+                       else (f"fsdp{world} ({'FULL_SHARD: parameters gathered per use into working slots' if args.fsdp_mode == 'full' else 'SHARD_GRAD_OP'}; "
+                             f"all-gather fused into the previous block's first tcgen05 GEMM; peer-memory "
+                             f"reduce-scatter {when}; fused AdamW shard)")
                        if args.parallel == "fsdp"
-                       else f"dp{world} (fused reduce-scatter / AdamW shard / all-gather)")
+                       else f"dp{world} (peer-memory reduce-scatter {when}; fused AdamW shard / all-gather)")
+    peak = torch.cuda.max_memory_allocated(device)
+    comm = getattr(getattr(trainer, "optimizer", None), "comm_bytes", None)
+    peak_gib = (peak + (comm() if comm is not None else 0)) / 2 ** 30
+    peak_gib = max_over_ranks(peak_gib, world)
     if rank == 0:
         out = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": W,
@@ -411,6 +425,7 @@ def main():
                        "l2": "no flush: per-step working set (weights + activations, several GB) >> 126 MB L2"},
             "clocks": clocks, "e2e": e2e, "gpu_launches": ours * K, "all_launches_per_step": total,
             "final_loss": final_loss,
+            "peak_mem_gib": round(peak_gib, 2),
         }
         if args.impl == "reference":
             out["impl"] = "reference"

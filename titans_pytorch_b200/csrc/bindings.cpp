@@ -78,11 +78,17 @@ void comm_adamw_shard(const at::Tensor& gsum, at::Tensor& master, at::Tensor& ex
                       const c10::optional<at::Tensor>& hyper, const c10::optional<at::Tensor>& seg_aux, int64_t me);
 void comm_reduce_segments(const at::Tensor& grad_ptrs, const at::Tensor& tab, int64_t nseg, int64_t items,
                           at::Tensor& gsum, double gscale, const at::Tensor& slot_ptrs, int64_t world, int64_t me);
+void comm_reduce_into(const at::Tensor& grad_ptrs, const at::Tensor& tab, int64_t nseg, int64_t items,
+                      at::Tensor& gsum, double gscale, at::Tensor& part, int64_t part_off, int64_t blocks,
+                      bool accumulate);
+void comm_norm_publish(const at::Tensor& part, int64_t nparts, const at::Tensor& slot_ptrs, int64_t world,
+                       int64_t me);
 // gemm_tc.cu
 at::Tensor gemm_tc(const at::Tensor& A, const at::Tensor& B);
 at::Tensor gemm_gather_tc(const at::Tensor& A, const at::Tensor& B, at::Tensor& flat, const at::Tensor& src_ptrs,
-                          int64_t u0, int64_t len, int64_t shard, int64_t me, bool consume);
-void fsdp_gather(at::Tensor& flat, const at::Tensor& src_ptrs, int64_t u0, int64_t len, int64_t shard, int64_t me);
+                          int64_t u0, int64_t len, int64_t shard, int64_t me, bool consume, bool copy_own);
+void fsdp_gather(at::Tensor& flat, const at::Tensor& src_ptrs, int64_t u0, int64_t len, int64_t shard, int64_t me,
+                 bool copy_own);
 // gemm_sm100.cu
 void gemm_sm100(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn, int64_t M, int64_t N, int64_t K,
                 int64_t mode, const at::Tensor& Cout, const c10::optional<at::Tensor>& R,
@@ -140,9 +146,14 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         pybind11::arg("step"), pybind11::arg("norm_out"), pybind11::arg("hyper") = pybind11::none(),
         pybind11::arg("seg_aux") = pybind11::none(), pybind11::arg("me") = 0);
   m.def("comm_reduce_segments", &tb::comm_reduce_segments);
+  m.def("comm_reduce_into", &tb::comm_reduce_into);
+  m.def("comm_norm_publish", &tb::comm_norm_publish);
   m.def("gemm_tc", &tb::gemm_tc);
-  m.def("gemm_gather_tc", &tb::gemm_gather_tc);
-  m.def("fsdp_gather", &tb::fsdp_gather);
+  m.def("gemm_gather_tc", &tb::gemm_gather_tc, pybind11::arg("A"), pybind11::arg("B"), pybind11::arg("flat"),
+        pybind11::arg("src_ptrs"), pybind11::arg("u0"), pybind11::arg("len"), pybind11::arg("shard"),
+        pybind11::arg("me"), pybind11::arg("consume"), pybind11::arg("copy_own") = false);
+  m.def("fsdp_gather", &tb::fsdp_gather, pybind11::arg("flat"), pybind11::arg("src_ptrs"), pybind11::arg("u0"),
+        pybind11::arg("len"), pybind11::arg("shard"), pybind11::arg("me"), pybind11::arg("copy_own") = false);
   m.def("gemm_sm100", &tb::gemm_sm100, pybind11::arg("A"), pybind11::arg("a_mn"), pybind11::arg("B"),
         pybind11::arg("b_mn"), pybind11::arg("M"), pybind11::arg("N"), pybind11::arg("K"), pybind11::arg("mode"),
         pybind11::arg("C"), pybind11::arg("R") = pybind11::none(), pybind11::arg("C2") = pybind11::none(),

@@ -90,10 +90,13 @@ __global__ void reduce_shard_kernel(const __nv_bfloat16* const* __restrict__ gra
 // Segment form (sharded-parameter layout): for segment s = (flat offset,
 // shard offset, length), g[shard_off + i] = sum_r G_r[flat_off + i]; work
 // items are kChunk-element pieces of the segments.
+// `accumulate`: g[shard_off + i] += the sum (gradient accumulation over
+// micro-batches whose gradients are reduced one by one); the partial norms
+// are those of the accumulated values.
 __global__ void reduce_segments_kernel(const __nv_bfloat16* const* __restrict__ grads,
                                        const int64_t* __restrict__ segs, const int64_t* __restrict__ item_start,
                                        int nseg, int64_t nitems, int world, float* __restrict__ gsum, float gscale,
-                                       float* __restrict__ part);
+                                       float* __restrict__ part, int accumulate);
 
 // single block: slot[me] of every peer <- sum(part)
 __global__ void norm_publish_kernel(const float* __restrict__ part, int nparts, float* const* __restrict__ slots,
@@ -127,7 +130,7 @@ __device__ __forceinline__ int find_seg(const int64_t* __restrict__ item_start, 
 __global__ void reduce_segments_kernel(const __nv_bfloat16* const* __restrict__ grads,
                                        const int64_t* __restrict__ segs, const int64_t* __restrict__ item_start,
                                        int nseg, int64_t nitems, int world, float* __restrict__ gsum, float gscale,
-                                       float* __restrict__ part) {
+                                       float* __restrict__ part, int accumulate) {
   __shared__ float red[32];
   float acc = 0.f;
   for (int64_t it = blockIdx.x; it < nitems; it += gridDim.x) {
@@ -143,6 +146,11 @@ __global__ void reduce_segments_kernel(const __nv_bfloat16* const* __restrict__ 
         for (int k = 0; k < 8; ++k) sum[k] += x[k];
       }
       float4* dst = reinterpret_cast<float4*>(gsum + soff + e);
+      if (accumulate) {
+        const float4 a = dst[0], b = dst[1];
+        sum[0] += a.x; sum[1] += a.y; sum[2] += a.z; sum[3] += a.w;
+        sum[4] += b.x; sum[5] += b.y; sum[6] += b.z; sum[7] += b.w;
+      }
       dst[0] = make_float4(sum[0], sum[1], sum[2], sum[3]);
       dst[1] = make_float4(sum[4], sum[5], sum[6], sum[7]);
 #pragma unroll
@@ -217,6 +225,8 @@ __global__ void adamw_shard_kernel(const float* __restrict__ gsum, float* __rest
 }  // namespace comm
 
 // ---------------------------------------------------------------- host API
+
+static int64_t world_of(const at::Tensor& ptrs) { return ptrs.numel(); }
 
 // Peer-shareable device buffer: cudaMalloc'd (not from PyTorch's caching
 // allocator, so its IPC handle covers exactly this buffer).  Returns the
@@ -311,12 +321,45 @@ void comm_reduce_segments(const at::Tensor& grad_ptrs, const at::Tensor& tab, in
     const int64_t* segs = tab.data_ptr<int64_t>();
     comm::reduce_segments_kernel<<<blocks, 256, 0, stream()>>>(
         reinterpret_cast<const __nv_bfloat16* const*>(grad_ptrs.data_ptr<int64_t>()), segs, segs + 3 * nseg,
-        (int)nseg, items, (int)world, gsum.data_ptr<float>(), (float)gscale, part.data_ptr<float>());
+        (int)nseg, items, (int)world, gsum.data_ptr<float>(), (float)gscale, part.data_ptr<float>(), 0);
   }
   comm::norm_publish_kernel<<<1, 256, 0, stream()>>>(part.data_ptr<float>(), blocks,
                                                      reinterpret_cast<float* const*>(slot_ptrs.data_ptr<int64_t>()),
                                                      (int)world, (int)me);
   check_launch("comm_reduce_segments");
+}
+
+// Reduce-scatter of one unit's gradients without publishing the norm:
+// block partials of the squared norm go to part[part_off, part_off + blocks)
+// (`blocks` fixed by the caller, so every unit's slice of `part` is fixed and
+// the launches are identical every step).  Runs on any stream (e.g. a
+// communication stream while the backward of earlier layers continues).
+void comm_reduce_into(const at::Tensor& grad_ptrs, const at::Tensor& tab, int64_t nseg, int64_t items,
+                      at::Tensor& gsum, double gscale, at::Tensor& part, int64_t part_off, int64_t blocks,
+                      bool accumulate) {
+  TORCH_CHECK(part.is_cuda() && part.scalar_type() == at::kFloat && part_off >= 0 && blocks > 0 &&
+                  part_off + blocks <= part.numel(),
+              "comm_reduce_into: partial-norm slice out of range");
+  if (nseg == 0 || items == 0) {
+    part.narrow(0, part_off, blocks).zero_();
+    return;
+  }
+  const int64_t* segs = tab.data_ptr<int64_t>();
+  comm::reduce_segments_kernel<<<(int)blocks, 256, 0, stream()>>>(
+      reinterpret_cast<const __nv_bfloat16* const*>(grad_ptrs.data_ptr<int64_t>()), segs, segs + 3 * nseg,
+      (int)nseg, items, (int)world_of(grad_ptrs), gsum.data_ptr<float>(), (float)gscale,
+      part.data_ptr<float>() + part_off, accumulate ? 1 : 0);
+  check_launch("comm_reduce_into");
+}
+
+// slot[me] of every peer <- sum(part[0, nparts))
+void comm_norm_publish(const at::Tensor& part, int64_t nparts, const at::Tensor& slot_ptrs, int64_t world,
+                       int64_t me) {
+  TORCH_CHECK(nparts > 0 && nparts <= part.numel(), "comm_norm_publish: nparts");
+  comm::norm_publish_kernel<<<1, 256, 0, stream()>>>(part.data_ptr<float>(), (int)nparts,
+                                                     reinterpret_cast<float* const*>(slot_ptrs.data_ptr<int64_t>()),
+                                                     (int)world, (int)me);
+  check_launch("comm_norm_publish");
 }
 
 }  // namespace tb

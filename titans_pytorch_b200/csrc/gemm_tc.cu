@@ -66,6 +66,8 @@ struct Gather {
                                     // before launch); nullptr: B is not waited for
   int64_t u0, len, shard, w0;       // unit [u0, u0 + len); rank r owns [r * shard, (r + 1) * shard); B at w0
   int world, me;
+  int copy_own;                     // also copy this rank's own part (the unit's destination is a working
+                                    // slot, its source this rank's shard store)
 };
 
 __device__ __forceinline__ uint32_t ld_acquire_gpu(const unsigned* p) {
@@ -261,7 +263,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       for (int64_t e = e0; e < e1;) {
         const int owner = (int)(e / g.shard);
         const int64_t se = min(e1, (int64_t)(owner + 1) * g.shard);
-        if (owner != g.me) bytes += (uint32_t)((se - e) * 2);
+        if (owner != g.me || g.copy_own) bytes += (uint32_t)((se - e) * 2);
         e = se;
       }
       if (bytes == 0) return 0;
@@ -269,7 +271,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       for (int64_t e = e0; e < e1;) {
         const int owner = (int)(e / g.shard);
         const int64_t se = min(e1, (int64_t)(owner + 1) * g.shard);
-        if (owner != g.me)
+        if (owner != g.me || g.copy_own)
           tc::bulk_load(smem + OFF_G + b * PIECE_BYTES + (e - e0) * 2, g.src[owner] + g.u0 + e, (uint32_t)((se - e) * 2),
                         bar_g + b);
         e = se;
@@ -299,7 +301,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           for (int64_t e = e0; e < e1;) {
             const int owner = (int)(e / g.shard);
             const int64_t se = min(e1, (int64_t)(owner + 1) * g.shard);
-            if (owner != g.me) bulk_store(g.dst + g.u0 + e, smem + OFF_G + b * PIECE_BYTES + (e - e0) * 2,
+            if (owner != g.me || g.copy_own) bulk_store(g.dst + g.u0 + e, smem + OFF_G + b * PIECE_BYTES + (e - e0) * 2,
                                           (uint32_t)((se - e) * 2));
             e = se;
           }
@@ -393,7 +395,7 @@ at::Tensor gemm_tc(const at::Tensor& A, const at::Tensor& B) {
 // unit and its tiles wait for their rows; otherwise B is any local tensor
 // (prefetch of another layer's parameters).
 at::Tensor gemm_gather_tc(const at::Tensor& A, const at::Tensor& B, at::Tensor& flat, const at::Tensor& src_ptrs,
-                          int64_t u0, int64_t len, int64_t shard, int64_t me, bool consume) {
+                          int64_t u0, int64_t len, int64_t shard, int64_t me, bool consume, bool copy_own) {
   const at::cuda::CUDAGuard guard(A.device());
   check_operand(A, "A");
   check_operand(B, "B");
@@ -426,6 +428,7 @@ at::Tensor gemm_gather_tc(const at::Tensor& A, const at::Tensor& B, at::Tensor& 
   g.w0 = consume ? w0 : u0;
   g.world = world;
   g.me = (int)me;
+  g.copy_own = copy_own ? 1 : 0;
   launch_gemm(A, bp, Cout, (int)M, (int)N, (int)K, g, A.device());
   check_launch("gemm_gather_tc");
   return Cout;
@@ -434,21 +437,24 @@ at::Tensor gemm_gather_tc(const at::Tensor& A, const at::Tensor& B, at::Tensor& 
 namespace fsdp {
 
 // Plain all-gather of a unit: this rank's buffer <- the owners' buffers,
-// 16 bytes per thread per step, own range skipped.
+// 16 bytes per thread per step, own range skipped unless `copy_own`.
 __global__ void gather_kernel(const __nv_bfloat16* const* __restrict__ src, __nv_bfloat16* __restrict__ dst,
-                              int64_t u0, int64_t len, int64_t shard, int me) {
+                              int64_t u0, int64_t len, int64_t shard, int me, int copy_own) {
   const int64_t nv = len / 8;
   for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < nv; v += (int64_t)gridDim.x * blockDim.x) {
     const int64_t e = v * 8;
     const int owner = (int)(e / shard);
-    if (owner == me) continue;
+    if (owner == me && !copy_own) continue;
     *reinterpret_cast<uint4*>(dst + u0 + e) = *reinterpret_cast<const uint4*>(src[owner] + u0 + e);
   }
 }
 
 }  // namespace fsdp
 
-void fsdp_gather(at::Tensor& flat, const at::Tensor& src_ptrs, int64_t u0, int64_t len, int64_t shard, int64_t me) {
+// `src_ptrs[r] + u0 + e` is where owner r keeps unit element e (a caller can
+// offset the pointers so the owners' parts come from a compact shard store).
+void fsdp_gather(at::Tensor& flat, const at::Tensor& src_ptrs, int64_t u0, int64_t len, int64_t shard, int64_t me,
+                 bool copy_own) {
   const at::cuda::CUDAGuard guard(flat.device());
   TORCH_CHECK(flat.is_cuda() && flat.scalar_type() == at::kBFloat16 && flat.is_contiguous() && aligned16(flat),
               "fsdp_gather: flat must be a contiguous bf16 CUDA buffer");
@@ -459,7 +465,7 @@ void fsdp_gather(at::Tensor& flat, const at::Tensor& src_ptrs, int64_t u0, int64
   const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>((len / 8 + 255) / 256, (int64_t)num_sms() * 8));
   fsdp::gather_kernel<<<blocks, 256, 0, stream()>>>(
       reinterpret_cast<const __nv_bfloat16* const*>(src_ptrs.data_ptr<int64_t>()), (__nv_bfloat16*)flat.data_ptr(),
-      u0, len, shard, (int)me);
+      u0, len, shard, (int)me, copy_own ? 1 : 0);
   check_launch("fsdp_gather");
 }
 

@@ -27,6 +27,7 @@ import torch
 import torch.distributed as dist
 
 from ..ops._ext import ext
+from .peer import PeerBuffer
 from ..train.optim import (ALIGN, FlatParamSpace, FusedAdamW, intersect_segments, segment_table,
                            unique_trainable)
 
@@ -42,30 +43,7 @@ class DPFusedAdamW(FusedAdamW):
         return 1.0 / self.world_size
 
 
-class _PeerBuffer:
-    """A cudaMalloc'd buffer of every rank, mapped into this process."""
-
-    def __init__(self, nbytes: int, device: torch.device, group, world: int, rank: int):
-        E = ext()
-        self.local, handle = E.comm_alloc(int(nbytes), device.index)
-        handles = [None] * world
-        dist.all_gather_object(handles, bytes(handle.tolist()), group=group)
-        self.opened = []
-        ptrs = []
-        for r, h in enumerate(handles):
-            if r == rank:
-                ptrs.append(self.local.data_ptr())
-            else:
-                p = E.comm_ipc_open(torch.tensor(list(h), dtype=torch.uint8), device.index)
-                self.opened.append(p)
-                ptrs.append(p)
-        self.ptrs = torch.tensor(ptrs, dtype=torch.int64, device=device)
-
-    def close(self):
-        E = ext()
-        for p in self.opened:
-            E.comm_ipc_close(p)
-        self.opened = []
+_PeerBuffer = PeerBuffer  # kept for callers of the former name
 
 
 class FusedDPAdamW(FusedAdamW):
@@ -155,6 +133,10 @@ class FusedDPAdamW(FusedAdamW):
         E.comm_barrier(self.sig.ptrs, 2, self.epoch, False, w, me, self.err)  # every rank's weights written
         return loss
 
+    def comm_bytes(self) -> int:
+        """Device bytes held outside PyTorch's allocator (the peer-visible buffers)."""
+        return sum(b.nbytes for b in self._bufs)
+
     def check_errors(self) -> None:
         """Raise if a bounded cross-GPU wait ran out (reads a device word: synchronises)."""
         v = int(self.err.item())
@@ -182,7 +164,18 @@ class FusedDPAdamW(FusedAdamW):
 
 
 class DataParallelEngine:
-    def __init__(self, group=None, reduce: str | None = None) -> None:
+    """Engine for :class:`~titans_pytorch_b200.train.trainer.Trainer` (``engine=``).
+
+    ``reduce="fused"`` with ``overlap=True`` (default): the optimizer state is
+    sharded per block (:class:`~titans_pytorch_b200.parallel.fsdp.FSDPAdamW`
+    with every unit replicated) and each block's gradients are reduce-scattered
+    over peer memory on a communication stream as soon as the backward has
+    finished with the block, while the earlier blocks' backward runs (DDP's
+    bucketed all-reduce from autograd hooks); clip, AdamW and the all-gather
+    by peer stores follow at the step.  ``overlap=False``: one contiguous
+    shard per rank, reduced after the backward (:class:`FusedDPAdamW`)."""
+
+    def __init__(self, group=None, reduce: str | None = None, overlap: bool = True) -> None:
         if not dist.is_initialized():
             raise RuntimeError("DataParallelEngine needs an initialised process group")
         self.group = group
@@ -193,10 +186,16 @@ class DataParallelEngine:
         if reduce not in ("fused", "collective"):
             raise ValueError("reduce must be 'fused' or 'collective'")
         self.reduce = reduce
+        self.overlap = overlap
 
     def make_optimizer(self, model: torch.nn.Module, cfg):
         if self.reduce == "fused" and next(model.parameters()).dtype != torch.bfloat16:
             self.reduce = "collective"  # the peer-memory path exchanges bf16 weights and gradients
+        if self.reduce == "fused" and self.overlap:
+            from .fsdp import FSDPAdamW
+
+            return FSDPAdamW(model, cfg, self.group, fused=True, reshard=False, replicate_units=True,
+                             overlap=True)
         if self.reduce == "fused":
             return FusedDPAdamW(model, cfg, self.group)
         opt = DPFusedAdamW(model.parameters(), lr=cfg.lr, betas=cfg.betas, eps=cfg.eps,

@@ -56,10 +56,16 @@ class FlatParamSpace:
     """Owns the flat parameter and gradient buffers of a set of parameters."""
 
     def __init__(self, params, grad_dtype: torch.dtype | None = None, pad_to: int = 1,
-                 buffers=None) -> None:
+                 buffers=None, placement=None) -> None:
         """``pad_to``: round the total length up to a multiple of it (e.g. ALIGN*world for
         sharding).  ``buffers``: optional callable ``(total, dtype) -> (flat, grad)`` that
-        provides the two flat buffers (e.g. peer-visible memory); zero-filled."""
+        provides the two flat buffers (e.g. peer-visible memory); zero-filled.
+
+        ``placement``: optional ``(phys, total)``: parameter i lives at ``phys[i]`` of
+        buffers of ``total`` elements instead of its logical offset (parameters may
+        share memory, e.g. the working slots of a sharded-parameter engine; their
+        values are then not copied in).  ``offsets`` stay logical (optimizer
+        bookkeeping, ``active_segments``); ``phys`` is where the views point."""
         plist = unique_trainable(params)
         self.params = plist
         self.device = plist[0].device
@@ -70,16 +76,27 @@ class FlatParamSpace:
         for p in plist:
             self.offsets.append(off)
             off += (p.numel() + ALIGN - 1) // ALIGN * ALIGN
-        self.total = (off + pad_to - 1) // pad_to * pad_to
+        self.logical_total = off
+        if placement is None:
+            self.phys = list(self.offsets)
+            self.total = (off + pad_to - 1) // pad_to * pad_to
+            copy_in = [True] * len(plist)
+        else:
+            self.phys, self.total = list(placement[0]), int(placement[1])
+            counts: dict[int, int] = {}
+            for o in self.phys:
+                counts[o] = counts.get(o, 0) + 1
+            copy_in = [counts[o] == 1 for o in self.phys]
         if buffers is not None:
             self.flat, self.grad = buffers(self.total, self.dtype)
         else:
             self.flat = torch.zeros(self.total, dtype=self.dtype, device=self.device)
             self.grad = torch.zeros(self.total, dtype=grad_dtype or self.dtype, device=self.device)
         with torch.no_grad():
-            for p, o in zip(plist, self.offsets):
+            for p, o, cp in zip(plist, self.phys, copy_in, strict=True):
                 n = p.numel()
-                self.flat[o:o + n].copy_(p.detach().reshape(-1))
+                if cp:
+                    self.flat[o:o + n].copy_(p.detach().reshape(-1))
                 p.data = self.flat[o:o + n].view_as(p)
                 p.grad = self.grad[o:o + n].view_as(p)
         self.got = [False] * len(plist)
@@ -95,7 +112,7 @@ class FlatParamSpace:
 
     def rebind_grads(self) -> None:
         """Re-attach the flat gradient views (after a caller set .grad = None)."""
-        for p, o in zip(self.params, self.offsets):
+        for p, o in zip(self.params, self.phys):
             if p.grad is None or p.grad.data_ptr() != self.grad[o:o + 1].data_ptr():
                 p.grad = self.grad[o:o + p.numel()].view_as(p)
 

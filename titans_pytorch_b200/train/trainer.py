@@ -107,6 +107,9 @@ class Trainer:
         labels = self._to_device(batch["labels"])
         accum = self.cfg.gradient_accumulation_steps
         loss = self.loss_fn(ids, labels)
+        prep = getattr(self.optimizer, "prepare_backward", None)
+        if prep is not None:  # engines that reduce during the backward: is this the step's last one?
+            prep((self._micro + 1) % accum == 0)
         with accumulate_weight_grads():
             (loss / accum if accum > 1 else loss).backward()
         self._micro += 1

@@ -61,11 +61,14 @@ def save_checkpoint(path: str, model: torch.nn.Module, optimizer=None, scheduler
                     epoch: int = 0, best_val_loss: float = float("inf"), model_type: str | None = None,
                     tokenizer_name: str | None = None, data_position: int | None = None,
                     train_config: dict | None = None, dtype: torch.dtype | None = None,
-                    extra: dict | None = None) -> str:
-    """Write a reference-loadable checkpoint (plus resume state) to ``path``."""
+                    extra: dict | None = None, state_dict: dict | None = None) -> str:
+    """Write a reference-loadable checkpoint (plus resume state) to ``path``
+    (``state_dict``: the model's values when ``model.state_dict()`` does not
+    hold them, e.g. parameters sharded over ranks)."""
     cfg: TitansConfig = model.config
+    src = model.state_dict() if state_dict is None else state_dict
     sd = {k: (v.to(dtype) if dtype is not None and v.is_floating_point() else v).detach().cpu()
-          for k, v in model.state_dict().items()}
+          for k, v in src.items()}
     ckpt = {
         "model_state_dict": sd,
         "optimizer_state_dict": optimizer.state_dict() if optimizer is not None else None,
@@ -119,16 +122,21 @@ def save_training_checkpoint(path: str, trainer, *, rank: int = 0, world: int = 
     files are on disk (the fused data-parallel step's device barriers have a
     time budget, and a long write on rank 0 must not run it out)."""
     opt = trainer.optimizer
-    mat = getattr(opt, "materialize", None)
-    if mat is not None:
-        mat()
+    full = getattr(opt, "full_model_state_dict", None)
+    model_sd = None
+    if full is not None:  # every rank takes part in the gathers of sharded units
+        model_sd = full(trainer.model)
+    else:
+        mat = getattr(opt, "materialize", None)
+        if mat is not None:
+            mat()
     sharded = world > 1 and getattr(opt, "shard_state", False)
     if sharded:
         sd = {k: (v.detach().cpu() if isinstance(v, torch.Tensor) else v) for k, v in opt.state_dict().items()}
         _atomic_save(sd, shard_path(path, rank, world))
     if rank == 0:
         save_checkpoint(path, trainer.model, None if sharded else opt, trainer.scheduler,
-                        extra={"optimizer_shards": world if sharded else 0}, **meta)
+                        extra={"optimizer_shards": world if sharded else 0}, state_dict=model_sd, **meta)
     _barrier(group)
     return path
 

@@ -83,6 +83,9 @@ void comm_reduce_into(const at::Tensor& grad_ptrs, const at::Tensor& tab, int64_
                       bool accumulate);
 void comm_norm_publish(const at::Tensor& part, int64_t nparts, const at::Tensor& slot_ptrs, int64_t world,
                        int64_t me);
+std::vector<at::Tensor> quantize_int8_rows(const at::Tensor& w);
+at::Tensor dequantize_int8_rows(const at::Tensor& q, const at::Tensor& s);
+at::Tensor int8_gemm_small(const at::Tensor& x, const at::Tensor& q, const at::Tensor& s);
 // gemm_tc.cu
 at::Tensor gemm_tc(const at::Tensor& A, const at::Tensor& B);
 at::Tensor gemm_gather_tc(const at::Tensor& A, const at::Tensor& B, at::Tensor& flat, const at::Tensor& src_ptrs,
@@ -148,6 +151,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("comm_reduce_segments", &tb::comm_reduce_segments);
   m.def("comm_reduce_into", &tb::comm_reduce_into);
   m.def("comm_norm_publish", &tb::comm_norm_publish);
+  m.def("quantize_int8_rows", &tb::quantize_int8_rows);
+  m.def("dequantize_int8_rows", &tb::dequantize_int8_rows);
+  m.def("int8_gemm_small", &tb::int8_gemm_small);
   m.def("gemm_tc", &tb::gemm_tc);
   m.def("gemm_gather_tc", &tb::gemm_gather_tc, pybind11::arg("A"), pybind11::arg("B"), pybind11::arg("flat"),
         pybind11::arg("src_ptrs"), pybind11::arg("u0"), pybind11::arg("len"), pybind11::arg("shard"),

@@ -284,14 +284,18 @@ class ContinuousBatcher:
 # ------------------------------------------------------------- quantization
 @torch.no_grad()
 def quantize_model_dynamic(model, bits: int = 8):
-    """Weight-only symmetric per-output-channel quantization of every Linear weight.
+    """Weight-only symmetric per-output-channel quantization (the reference's
+    ``quantize_model_dynamic``, `optimized_inference.py:481-536`).
 
-    The weights are rounded to the ``bits``-bit grid and stored back in their
-    dtype (the kernels compute in bf16), so memory is unchanged but the model's
-    numerics are those of the quantized weights.  (The reference's int8 path,
-    `optimized_inference.py:481-536`, relies on torch's CPU-only dynamic
-    quantization, which does not apply to sm_100a kernels.)
+    ``bits=8``: real int8 weights (:func:`~titans_pytorch_b200.ops.quant.quantize_model_int8`):
+    half the bf16 bytes in memory, dequantised inside the int8 GEMM.  Other
+    widths round the weights to the ``bits``-bit grid and store them back in
+    their dtype (the numerics of the quantized weights, no memory saving).
     """
+    if bits == 8:
+        from ..ops.quant import quantize_model_int8
+
+        return quantize_model_int8(model)
     qmax = 2 ** (bits - 1) - 1
     for m in model.modules():
         if isinstance(m, torch.nn.Linear):

@@ -80,12 +80,16 @@ def swiglu_ffn(x: torch.Tensor, w_gate: torch.Tensor, w_up: torch.Tensor, w_down
     """``[residual +] down(silu(x Wg^T) * (x Wu^T))`` (dropout on the hidden activation in training)."""
     drop = dropout_p > 0.0 and training
     F_ = w_gate.shape[0]
-    if (not drop and kernel_ok(x, w_gate, use_kernels) and F_ % 32 == 0 and w_up.dtype == torch.bfloat16
+    int8 = any(type(w).__name__ == "Int8Weight" for w in (w_gate, w_up, w_down))
+    if (not drop and not int8 and kernel_ok(x, w_gate, use_kernels) and F_ % 32 == 0 and w_up.dtype == torch.bfloat16
             and w_down.dtype == torch.bfloat16 and w_down.shape[0] % 8 == 0 and x.numel() > 0
             and (residual is None or (residual.dtype == torch.bfloat16 and residual.shape == x.shape[:-1]
                                       + (w_down.shape[0],)))):
         return _FusedFFN.apply(x, residual, w_gate, w_up, w_down)
-    if want_kernels(x, use_kernels):
+    if int8 and not want_kernels(x, use_kernels):
+        gu = linear(x, w_gate, w_up, use_kernels=use_kernels)
+        h = F.silu(gu[..., :F_]) * gu[..., F_:]
+    elif want_kernels(x, use_kernels):
         gu = linear(x, w_gate, w_up, use_kernels=use_kernels)
         h = _SwiGLUFn.apply(gu.view(-1, gu.shape[-1])).view(*x.shape[:-1], F_)
     else:

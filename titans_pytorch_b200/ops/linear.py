@@ -178,7 +178,11 @@ class _Linear(torch.autograd.Function):
 
 
 def linear(x: torch.Tensor, *weights: torch.Tensor, use_kernels: bool | None = None) -> torch.Tensor:
-    """``x @ cat(weights)^T`` (no bias)."""
+    """``x @ cat(weights)^T`` (no bias).  Int8 weights (``ops.quant``) run the int8 GEMM."""
+    if any(type(w).__name__ == "Int8Weight" for w in weights):
+        from .quant import int8_linear
+
+        return int8_linear(x, weights)
     kern = kernel_ok(x, weights[0], use_kernels) and all(w.dtype == torch.bfloat16 for w in weights) and all(
         w.shape[1] == x.shape[-1] and w.shape[0] % 8 == 0 for w in weights)
     if not torch.is_grad_enabled() or not any(w.requires_grad for w in weights):

@@ -317,9 +317,10 @@ def main():
     ap.add_argument("--parallel", choices=["dp", "fsdp"], default="dp",
                     help="N > 1, this framework: dp = replicated weights, optimizer state sharded; fsdp = "
                          "parameters sharded per block, all-gathered inside the first GEMM of the previous block")
-    ap.add_argument("--no-overlap", action="store_true",
-                    help="N > 1, this framework: reduce the gradients after the backward instead of per block "
-                         "during it")
+    ap.add_argument("--overlap", choices=["auto", "on", "off"], default="auto",
+                    help="N > 1, this framework: reduce-scatter each block's gradients on a communication stream "
+                         "during the backward (on) or after it (off); auto = off for dp (measured faster), on "
+                         "for fsdp")
     ap.add_argument("--fsdp-mode", choices=["full", "grad-op"], default="full",
                     help="fsdp: full = FULL_SHARD (parameters gathered per use into working slots, gradients "
                          "reduce-scattered per block during the backward); grad-op = SHARD_GRAD_OP (gathered "
@@ -346,7 +347,8 @@ def main():
         trainer, nparams = built
         prefixes = ()
     else:
-        trainer, nparams = build_ours(device, world, args.parallel, overlap=not args.no_overlap,
+        overlap = args.overlap == "on" or (args.overlap == "auto" and args.parallel == "fsdp")
+        trainer, nparams = build_ours(device, world, args.parallel, overlap=overlap,
                                       reshard=args.fsdp_mode == "full")
         prefixes = ("tb::",)
 
@@ -403,7 +405,8 @@ def main():
     tokens = world * MICRO_BATCH * SEQ
     value = tokens / (ms / 1000)
     parallelism = f"dp{world}"
-    when = "after the backward" if args.no_overlap else "per block during the backward"
+    overlapped = args.overlap == "on" or (args.overlap == "auto" and args.parallel == "fsdp")
+    when = "per block during the backward" if overlapped else "after the backward"
     if world > 1:
         parallelism = (f"dp{world} (grads all-reduced after backward)" if args.impl == "reference"
                        else (f"fsdp{world} ({'FULL_SHARD: parameters gathered per use into working slots' if args.fsdp_mode == 'full' else 'SHARD_GRAD_OP'}; "

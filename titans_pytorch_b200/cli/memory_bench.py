@@ -58,6 +58,11 @@ def main(argv=None) -> None:
     add("--dim", type=int, default=64)
     add("--hidden", type=int, default=256)
     add("--chunk", type=int, default=64)
+    add("--mode", choices=["paper", "ref"], default="paper",
+        help="paper: the chunked per-head scan above; ref: one reference-semantics update of a "
+             "block's memory (memory_step: MLP forward on the keys, scaled error, back-propagation, "
+             "gated update in the weight-gradient epilogues) at a training workload's shape")
+    add("--shape", choices=["mag170m", "mal760m"], default="mag170m", help="--mode ref: workload shape")
     add("--warmup", type=int, default=1)
     add("--steps", type=int, default=3)
     add("--peak-tflops", type=float, default=None, help="bf16 GEMM burst peak (default: the measured one)")
@@ -69,6 +74,9 @@ def main(argv=None) -> None:
         a.peak_tflops = peaks["bf16_tflops"]
     if getattr(a, "peak_gbs", 0) is None:
         a.peak_gbs = peaks["hbm_gbs"]
+    if a.mode == "ref":
+        ref_update(a)
+        return
     from ..ops.memory_paper import memory_scan
 
     dev = torch.device("cuda")
@@ -104,6 +112,64 @@ def main(argv=None) -> None:
 
         rec["kernel_error_status"] = int(ext().kernel_error_status(0, True))
     print(json.dumps(rec))
+
+
+REF_SHAPES = {  # tokens per update (micro-batch x sequence), dim, memory hidden width, memory depth
+    "mag170m": dict(B=8, T=4096, D=768, hidden=3072, L=2),
+    "mal760m": dict(B=1, T=16384, D=1536, hidden=6144, L=3),
+}
+
+
+def ref_update(a) -> None:
+    """Time ``memory_step`` (reference semantics) at a training workload's shape.
+
+    FLOPs = 2 N (3 S - d0 d1) with N tokens and S = sum of the layers' d_i d_{i+1}:
+    the forward GEMMs, every weight-gradient GEMM, and the input-gradient GEMMs
+    of all layers but the first; the bound is compute (all GEMMs are large),
+    so the roofline time is FLOPs / the measured bf16 peak."""
+    from ..ops._ext import ext
+    from ..ops.memory import memory_step
+
+    sh = REF_SHAPES[a.shape]
+    B, T, D, Hd, L = sh["B"], sh["T"], sh["D"], sh["hidden"], sh["L"]
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev).manual_seed(0)
+    bf = torch.bfloat16
+    k = torch.nn.functional.normalize(torch.randn(B, T, D, device=dev, generator=g), dim=-1).to(bf)
+    v = torch.randn(B, T, D, device=dev, generator=g).to(bf)
+    x = torch.randn(B, T, D, device=dev, generator=g).to(bf)
+    dims = [D] + [Hd] * (L - 1) + [D]
+    ws = [(0.02 * torch.randn(dims[i + 1], dims[i], device=dev, generator=g)).to(bf) for i in range(L)]
+    ms = [torch.zeros_like(w) for w in ws]
+    gw = [(0.02 * torch.randn(D, D, device=dev, generator=g)).to(bf) for _ in range(3)]
+    gb = [torch.zeros(D, device=dev, dtype=bf) for _ in range(3)]
+
+    def step():
+        return memory_step(k, v, x, ws, ms, gw, gb, 0.1, 0.9, "silu")
+
+    for _ in range(max(1, a.warmup)):
+        step()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(a.steps):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        nw, nm = step()
+        e.record()
+        e.synchronize()
+        times.append(s.elapsed_time(e))
+    ms_ = statistics.median(times)
+    N = B * T
+    S = sum(dims[i] * dims[i + 1] for i in range(L))
+    flops = 2.0 * N * (3 * S - dims[0] * dims[1])
+    tf = flops / ms_ / 1e9
+    print(json.dumps({"bench": "memory_update_ref", "shape": a.shape, "ms": round(ms_, 4),
+                      "gflop": round(flops / 1e9, 1), "tflops": round(tf, 1),
+                      "frac_of_measured_peak": round(tf / a.peak_tflops, 3),
+                      "roofline_ms": round(flops / a.peak_tflops / 1e9, 4),
+                      "config": {"B": B, "T": T, "D": D, "hidden": Hd, "L_M": L},
+                      "state_finite": bool(all(torch.isfinite(t.float()).all() for t in nw + nm)),
+                      "kernel_error_status": int(ext().kernel_error_status(0, True))}))
 
 
 if __name__ == "__main__":

@@ -75,13 +75,6 @@ __device__ __forceinline__ unsigned range_bits(int lo, int hi) {
   const unsigned below_hi = hi >= 32 ? 0xffffffffu : ((1u << hi) - 1u);
   return below_hi & ~((1u << lo) - 1u);
 }
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
-        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
-}
 
 // K-major S-type product D = A B^T over the 96 head columns of two operand tiles
 __device__ __forceinline__ void mma_hd96(uint32_t d, uint32_t aA, uint32_t aB, uint32_t idesc) {
@@ -632,7 +625,7 @@ __global__ void __launch_bounds__(320, 1)
         float* dst = dQa + ((int64_t)bh * Tn + i) * HD + wg * 48;
         uint32_t v[32], v2[16];
         tc::tmem_ld32(tl + TQ_DQ + wg * 48, v);
-        tmem_ld16(tl + TQ_DQ + wg * 48 + 32, v2);
+        tc::tmem_ld16(tl + TQ_DQ + wg * 48 + 32, v2);
         tc::tmem_wait_ld();
         if (i < Tn) {
 #pragma unroll

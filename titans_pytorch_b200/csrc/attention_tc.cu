@@ -37,7 +37,6 @@ using bf16 = __nv_bfloat16;
 constexpr int BM = 128;  // rows per query tile
 constexpr int NQ = 2;    // query tiles per CTA
 constexpr int BN = 128;  // keys per tile
-constexpr int NS = 2;    // K/V stages
 constexpr int TILE_P = BM * BN * 2;
 
 // Shared-memory layout for head dim HD (64 or 96).  A Q/K/V tile holds
@@ -48,17 +47,21 @@ constexpr int TILE_P = BM * BN * 2;
 template <int HD>
 struct Fwd {
   static_assert(HD == 64 || HD == 96, "head_dim 64 or 96");
+  static constexpr int NS = HD == 64 ? 3 : 2;  // K/V stages (three fit at head dim 64)
   static constexpr int TILE_QA = BM * 64 * 2, TILE_QB = HD > 64 ? BM * 32 * 2 : 0, TILE_Q = TILE_QA + TILE_QB;
   static constexpr int TILE_KA = BN * 64 * 2, TILE_KB = HD > 64 ? BN * 32 * 2 : 0, TILE_K = TILE_KA + TILE_KB;
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_K = OFF_Q + NQ * TILE_Q;
   static constexpr int OFF_V = OFF_K + NS * TILE_K;
   static constexpr int OFF_P = OFF_V + NS * TILE_K;
-  static constexpr int OFF_BAR = OFF_P + NQ * TILE_P;
+  static constexpr int OFF_RED = OFF_P + NQ * TILE_P;  // [2 phases][NQ][2 halves][BM] fp32 row exchange
+  static constexpr int OFF_BAR = OFF_RED + 2 * NQ * 2 * BM * 4;
   static constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;
 };
 constexpr uint32_t TM_S = 0, TM_O = 256, TM_COLS = 512;
-constexpr int NTHREADS = 320;
+// warps 0-15: softmax (query tile = warp / 8, column half = (warp / 4) & 1); 16: producer; 17: MMA
+constexpr int SOFTMAX_WARPS = 16, PRODUCER_WARP = 16, MMA_WARP = 17;
+constexpr int NTHREADS = 32 * 18;
 
 __device__ __forceinline__ uint32_t pack2(float a, float b) {
   __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
@@ -142,6 +145,8 @@ __global__ void exp2_poly_eval_kernel(const float* __restrict__ x, float* __rest
 
 // tmQ/tmK/tmV: columns 0-63 (128-byte swizzle); tmQb/tmKb/tmVb: columns 64-95
 // (64-byte swizzle), used when HD = 96.
+// 18 warps: two of the four schedulers hold 5 warps, so 96 registers per thread
+// (5 x 32 x 96 <= 16,384 per scheduler)
 template <int HD>
 __global__ void __launch_bounds__(NTHREADS, 1)
     attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -152,6 +157,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   using C = Fwd<HD>;
+  constexpr int NS = C::NS;
   constexpr bool kSplit = HD > 64;  // columns 64-95 in a second, 64-byte-swizzled tile
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
   uint64_t* bar_q = bars + 0;
@@ -160,7 +166,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   uint64_t* bar_s_full = bars + 1 + 2 * NS;  // [NQ]
   uint64_t* bar_p_full = bars + 3 + 2 * NS;  // [NQ]
   uint64_t* bar_o_done = bars + 5 + 2 * NS;  // [NQ]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  uint64_t* bar_x = bars + 7 + 2 * NS;       // [NQ] row max / sum exchange between the two column halves
+  uint64_t* bar_s_free = bars + 9 + 2 * NS;  // [NQ] the row threads have read S (the next S may be issued)
+  static_assert(11 + 2 * NS <= 24, "forward barriers overlap the TMEM address word");
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 24);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -185,13 +194,15 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
     for (int q = 0; q < NQ; ++q) {
       tc::mbar_init(bar_s_full + q, 1);
-      tc::mbar_init(bar_p_full + q, 128);
+      tc::mbar_init(bar_p_full + q, 256);
       tc::mbar_init(bar_o_done + q, 1);
+      tc::mbar_init(bar_x + q, 256);
+      tc::mbar_init(bar_s_free + q, 256);
     }
     *abort_flag = 0;
     tc::mbar_fence_init();
   }
-  if (warp == 9) {
+  if (warp == MMA_WARP) {
     tc::tmem_alloc(tmem_slot, TM_COLS);
     tc::tmem_relinquish();
   }
@@ -200,7 +211,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   tc::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 8) {
+  if (warp == PRODUCER_WARP) {
     // ------------------------------------------------------------ producer
     if (lane == 0 && n_tiles > 0) {
       tc::tma_prefetch_desc(&tmQ);
@@ -232,7 +243,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           tc::mbar_wait(bar_kv_full + (it % NS), (it / NS) & 1, &keep_waiting, nullptr, 1ll << 27);
       }
     }
-  } else if (warp == 9) {
+  } else if (warp == MMA_WARP) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0 && n_tiles > 0) {
       constexpr uint32_t idesc_s = tc::idesc_bf16_f32(BM, BN, false, false);
@@ -260,11 +271,29 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         issue_s(0, 0);
         issue_s(1, 0);
       }
+      // Per key tile and query tile, head dim 64: the next tile's scores as soon
+      // as the row threads have read this tile's (so S(it+1) runs while they
+      // compute P(it)), then O += P V once P(it) is in shared memory.  Head dim
+      // 96: O += P V first (its S is 1.5x longer, and the next P store waits for
+      // this PV), then the next scores.
+      constexpr bool kEarlyS = HD == 64;
+      auto next_s = [&](int q, int it) -> bool {
+        if (q == 0 && !tc::mbar_wait(bar_kv_full + ((it + 1) % NS), ((it + 1) / NS) & 1, abort_flag, err))
+          return false;
+        if (!tc::mbar_wait(bar_s_free + q, it & 1, abort_flag, err)) return false;
+        tc::tc_fence_after();
+        issue_s(q, it + 1);
+        return true;
+      };
       for (int it = 0; ok && it < n_tiles; ++it) {
         const int s = it % NS;
         const bool more = it + 1 < n_tiles;
         const uint32_t aV = tc::smem_addr(smem + C::OFF_V + s * C::TILE_K);
         for (int q = 0; q < NQ && ok; ++q) {
+          if (kEarlyS && more && !next_s(q, it)) {
+            ok = false;
+            break;
+          }
           if (!tc::mbar_wait(bar_p_full + q, it & 1, abort_flag, err)) {
             ok = false;
             break;
@@ -283,27 +312,38 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           }
           tc::umma_commit(bar_o_done + q);
           if (q == NQ - 1) tc::umma_commit(bar_kv_empty + s);
-          if (more) {
-            if (q == 0) {
-              if (!tc::mbar_wait(bar_kv_full + ((it + 1) % NS), ((it + 1) / NS) & 1, abort_flag, err)) {
-                ok = false;
-                break;
-              }
-              tc::tc_fence_after();
-            }
-            issue_s(q, it + 1);
+          if (!kEarlyS && more && !next_s(q, it)) {
+            ok = false;
+            break;
           }
         }
       }
     }
   } else {
     // ------------------------------------------------------------ softmax
-    const int q = warp >> 2;              // query tile of this warpgroup
+    // Two warpgroups per query tile, one per 64-column half of the 128 keys:
+    // thread = (query row = TMEM lane, half).  The halves exchange their row
+    // max every tile (and their row sums at the end) through shared memory,
+    // synchronised by an mbarrier with a bounded wait; each half rescales and
+    // stores its half of the O columns.  S is released as soon as it is in
+    // registers, so the tensor core computes the next tile's scores meanwhile.
+    constexpr int HO = HD / 2;            // O columns per half (32 or 48)
+    const int q = warp >> 3;              // query tile of this warpgroup pair
+    const int hf = (warp >> 2) & 1;       // column half
     const int row = threadIdx.x & 127;    // TMEM lane
     const int i = m0 + q * BM + row;      // query index
+    const int c0 = hf * 64;               // first key column of this half
     const uint32_t tl = tmem + ((uint32_t)((warp & 3) * 32) << 16);
-    const uint32_t tS = tl + TM_S + q * BN, tO = tl + TM_O + q * HD;
-    uint8_t* sP = smem + C::OFF_P + q * TILE_P;
+    const uint32_t tS = tl + TM_S + q * BN + c0, tO = tl + TM_O + q * HD + hf * HO;
+    uint8_t* sP = smem + C::OFF_P + q * TILE_P + hf * (BM * 128);  // this half's 64-column K-major block
+    float* red = reinterpret_cast<float*>(smem + C::OFF_RED);
+    auto red_at = [&](int phase, int h) -> float* { return red + (((phase & 1) * NQ + q) * 2 + h) * BM + row; };
+    // this thread's O half: one 32-column load plus, for HD = 96, one 16-column load
+    auto o_load = [&](uint32_t (&r)[32], uint32_t (&r2)[16]) {
+      tc::tmem_ld32(tO, r);
+      if constexpr (HO > 32) tc::tmem_ld16(tO + 32, r2);
+      tc::tmem_wait_ld();
+    };
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
     const int win_lo = max(0, i - W + 1), win_hi = min(i, Tn - 1);  // visible main keys [win_lo, win_hi]
@@ -315,8 +355,72 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         break;
       }
       tc::tc_fence_after();
-      // PV(it-1) of this tile was issued before S(it), and the tensor pipe
-      // completes in order, so it is done by now: O is stable, the P buffer free
+      float s[64];
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        uint32_t r[32];
+        tc::tmem_ld32(tS + c * 32, r);
+#pragma unroll
+        for (int x = 0; x < 32; ++x) s[c * 32 + x] = __uint_as_float(r[x]);
+      }
+      tc::tmem_wait_ld();
+      tc::tc_fence_before();
+      tc::mbar_arrive(bar_s_free + q);  // S is in registers: the next tile's scores may be written
+      // visible tile columns: [0, pre_hi) are prefix keys; [lo2, hi2) the window
+      const int pre_hi = min(BN, max(0, P - n0));
+      const int lo2 = max(pre_hi, P - n0 + win_lo);
+      const int hi2 = min(BN, P - n0 + win_hi + 1);
+      unsigned vm[2];
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const int a = c0 + c * 32;
+        vm[c] = range_bits(-a, pre_hi - a) | range_bits(lo2 - a, hi2 - a);
+      }
+      const bool warp_full = __all_sync(0xffffffffu, (vm[0] & vm[1]) == 0xffffffffu);
+      // 32-column chunks no row of this warp can see skip the max and the exponentials (P = 0)
+      const unsigned vis_chunks = (__any_sync(0xffffffffu, vm[0] != 0u) ? 1u : 0u) |
+                                  (__any_sync(0xffffffffu, vm[1] != 0u) ? 2u : 0u);
+      float mx[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) mx[k] = -INFINITY;
+      if (warp_full) {
+#pragma unroll
+        for (int c = 0; c < 64; c += 2) mx[(c >> 1) & 7] = fmax3(mx[(c >> 1) & 7], s[c], s[c + 1]);
+      } else {
+#pragma unroll
+        for (int cc = 0; cc < 2; ++cc) {
+          if (!((vis_chunks >> cc) & 1u)) continue;
+#pragma unroll
+          for (int x = 0; x < 32; x += 2) {
+            const int c = cc * 32 + x;
+            s[c] = (vm[cc] >> x) & 1u ? s[c] : -INFINITY;
+            s[c + 1] = (vm[cc] >> (x + 1)) & 1u ? s[c + 1] : -INFINITY;
+            mx[(x >> 1) & 7] = fmax3(mx[(x >> 1) & 7], s[c], s[c + 1]);
+          }
+        }
+      }
+      float mraw = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                         fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+      // the row max over both halves
+      *red_at(it, hf) = mraw;
+      tc::mbar_arrive(bar_x + q);
+      ok = tc::mbar_wait(bar_x + q, it & 1, abort_flag, err);
+      if (!__all_sync(0xffffffffu, ok)) {
+        ok = false;
+        break;
+      }
+      mraw = fmaxf(mraw, *red_at(it, hf ^ 1));
+      // raw-score max; the softmax scale (> 0) is folded into one FFMA before ex2
+      const float m_cand = fmaxf(m_run, mraw * scale_log2);
+      // lazy rescale: the running max moves only when the tile's max exceeds it by
+      // more than 8 (log2 units), so P <= 2^8 and O is rescaled rarely
+      const bool grow = m_cand > m_run + 8.f;
+      const float m_new = grow ? m_cand : m_run;
+      const float m_use = m_new == -INFINITY ? 0.f : m_new;
+      const float corr = grow ? ex2(m_run - m_use) : 1.f;
+      // PV(it-1) of this query tile must be done before P(it) overwrites the P
+      // buffer and O is rescaled (it was issued when P(it-1) was ready, so it is
+      // normally complete by now; S(it+1) is already running on the tensor core)
       if (it > 0) {
         ok = tc::mbar_wait(bar_o_done + q, (it - 1) & 1, abort_flag, err);
         if (!__all_sync(0xffffffffu, ok)) {
@@ -325,75 +429,20 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         }
         tc::tc_fence_after();
       }
-      float s[BN];
-#pragma unroll
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t r[32];
-        tc::tmem_ld32(tS + c * 32, r);
-#pragma unroll
-        for (int x = 0; x < 32; ++x) s[c * 32 + x] = __uint_as_float(r[x]);
-      }
-      tc::tmem_wait_ld();
-      // visible columns: [0, pre_hi) are prefix keys; [lo2, hi2) the window
-      const int pre_hi = min(BN, max(0, P - n0));
-      const int lo2 = max(pre_hi, P - n0 + win_lo);
-      const int hi2 = min(BN, P - n0 + win_hi + 1);
-      const bool row_full = (pre_hi >= BN) || (lo2 <= pre_hi && pre_hi == 0 && lo2 <= 0 && hi2 >= BN);
-      const bool warp_full = __all_sync(0xffffffffu, row_full);
-      // 32-column chunks that some row of this warp can see (bit c); the others
-      // (beyond the diagonal, before the window, the non-prefix part of the
-      // prefix tile) skip the max and the exponentials and store P = 0
-      unsigned vis_chunks = 0;
-#pragma unroll
-      for (int c = 0; c < BN / 32; ++c) {
-        const int a = c * 32;
-        if (__any_sync(0xffffffffu, (a < pre_hi) || (a < hi2 && a + 32 > lo2))) vis_chunks |= 1u << c;
-      }
-      float mx[8];
-#pragma unroll
-      for (int k = 0; k < 8; ++k) mx[k] = -INFINITY;
-      if (warp_full) {
-        // every row of this warp sees the whole tile: no masking
-#pragma unroll
-        for (int c = 0; c < BN; c += 2) mx[(c >> 1) & 7] = fmax3(mx[(c >> 1) & 7], s[c], s[c + 1]);
-      } else {
-#pragma unroll
-        for (int cc = 0; cc < BN / 32; ++cc) {
-          if (!((vis_chunks >> cc) & 1u)) continue;
-          const int a = cc * 32;
-          const unsigned vm = range_bits(-a, pre_hi - a) | range_bits(lo2 - a, hi2 - a);
-#pragma unroll
-          for (int x = 0; x < 32; x += 2) {
-            const int c = a + x;
-            s[c] = (vm >> x) & 1u ? s[c] : -INFINITY;
-            s[c + 1] = (vm >> (x + 1)) & 1u ? s[c + 1] : -INFINITY;
-            mx[(x >> 1) & 7] = fmax3(mx[(x >> 1) & 7], s[c], s[c + 1]);
-          }
-        }
-      }
-      // raw-score max; the softmax scale (> 0) is folded into one FFMA before ex2
-      const float mraw = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
-                               fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
-      const float m_cand = fmaxf(m_run, mraw * scale_log2);
-      // lazy rescale: the running max moves only when the tile's max exceeds it by
-      // more than 8 (log2 units), so P <= 2^8 and O is rescaled rarely
-      const bool grow = m_cand > m_run + 8.f;
-      const float m_new = grow ? m_cand : m_run;
-      const float m_use = m_new == -INFINITY ? 0.f : m_new;
-      const float corr = grow ? ex2(m_run - m_use) : 1.f;
       uint64_t sm2[4] = {0ull, 0ull, 0ull, 0ull};  // packed partial row sums
       const uint64_t sc2 = f2(scale_log2, scale_log2), nm2 = f2(-m_use, -m_use);
       // P in 32-column pieces, each stored to shared memory (UMMA K-major) at once.
       // 6 of the 16 pairs of a piece are exponentiated on the FMA pipe, the
       // rest by MUFU, so neither unit alone sets the pace.
 #pragma unroll
-      for (int c = 0; c < BN; c += 32) {
+      for (int cc = 0; cc < 2; ++cc) {
         uint32_t pk[16];
-        if ((vis_chunks >> (c >> 5)) & 1u) {
+        if ((vis_chunks >> cc) & 1u) {
 #pragma unroll
           for (int x = 0; x < 32; x += 2) {
+            const int c = cc * 32 + x;
             float a, b, p0, p1;
-            f2split(ffma2(f2(s[c + x], s[c + x + 1]), sc2, nm2), a, b);
+            f2split(ffma2(f2(s[c], s[c + 1]), sc2, nm2), a, b);
             constexpr unsigned kPolyPairs = 0x2525u;  // pairs 0, 2, 5, 8, 10, 13 of 16
             if ((kPolyPairs >> (x >> 1)) & 1u) {
               exp2_poly2(a, b, p0, p1);
@@ -408,10 +457,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 #pragma unroll
           for (int x = 0; x < 16; ++x) pk[x] = 0u;
         }
-        uint8_t* blk = sP + (c >> 6) * (BM * 128) + row * 128;
+        uint8_t* blk = sP + row * 128;
 #pragma unroll
         for (int q4 = 0; q4 < 4; ++q4) {
-          const int ch = ((c >> 5) & 1) * 4 + q4;
+          const int ch = cc * 4 + q4;
           *reinterpret_cast<uint4*>(blk + ((ch ^ (row & 7)) << 4)) =
               make_uint4(pk[4 * q4], pk[4 * q4 + 1], pk[4 * q4 + 2], pk[4 * q4 + 3]);
         }
@@ -420,16 +469,17 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 #pragma unroll
       for (int k = 0; k < 4; ++k) f2split(sm2[k], sm[2 * k], sm[2 * k + 1]);
       const float rs = ((sm[0] + sm[1]) + (sm[2] + sm[3])) + ((sm[4] + sm[5]) + (sm[6] + sm[7]));
-      l_run = l_run * corr + rs;
+      l_run = l_run * corr + rs;  // this half's part of the row sum
       if (__any_sync(0xffffffffu, it > 0 && corr < 1.f)) {
+        uint32_t r[32], r2[16];
+        o_load(r, r2);
 #pragma unroll
-        for (int h = 0; h < HD / 32; ++h) {
-          uint32_t r[32];
-          tc::tmem_ld32(tO + h * 32, r);
-          tc::tmem_wait_ld();
+        for (int x = 0; x < 32; ++x) r[x] = __float_as_uint(__uint_as_float(r[x]) * corr);
+        tc::tmem_st32(tO, r);
+        if constexpr (HO > 32) {
 #pragma unroll
-          for (int x = 0; x < 32; ++x) r[x] = __float_as_uint(__uint_as_float(r[x]) * corr);
-          tc::tmem_st32(tO + h * 32, r);
+          for (int x = 0; x < 16; ++x) r2[x] = __float_as_uint(__uint_as_float(r2[x]) * corr);
+          tc::tmem_st16(tO + 32, r2);
         }
         tc::tmem_wait_st();
       }
@@ -441,15 +491,18 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     if (ok && n_tiles > 0) {
       ok = tc::mbar_wait(bar_o_done + q, (n_tiles - 1) & 1, abort_flag, err);
       if (__all_sync(0xffffffffu, ok)) {
-        tc::tc_fence_after();
-        const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-        const int bq = bh / H, hq = bh % H;
-        bf16* orow = O + (((int64_t)bq * Tn + i) * H + hq) * HD;
-#pragma unroll
-        for (int h = 0; h < HD / 32; ++h) {
-          uint32_t r[32];
-          tc::tmem_ld32(tO + h * 32, r);
-          tc::tmem_wait_ld();
+        // the row sum over both halves
+        *red_at(n_tiles, hf) = l_run;
+        tc::mbar_arrive(bar_x + q);
+        ok = tc::mbar_wait(bar_x + q, n_tiles & 1, abort_flag, err);
+        if (__all_sync(0xffffffffu, ok)) {
+          const float l_tot = l_run + *red_at(n_tiles, hf ^ 1);
+          tc::tc_fence_after();
+          const float inv = l_tot > 0.f ? 1.f / l_tot : 0.f;
+          const int bq = bh / H, hq = bh % H;
+          bf16* orow = O + (((int64_t)bq * Tn + i) * H + hq) * HD + hf * HO;
+          uint32_t r[32], r2[16];
+          o_load(r, r2);
           if (i < Tn) {
 #pragma unroll
             for (int x = 0; x < 32; x += 8) {
@@ -457,11 +510,21 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                                    pack2(__uint_as_float(r[x + 2]) * inv, __uint_as_float(r[x + 3]) * inv),
                                    pack2(__uint_as_float(r[x + 4]) * inv, __uint_as_float(r[x + 5]) * inv),
                                    pack2(__uint_as_float(r[x + 6]) * inv, __uint_as_float(r[x + 7]) * inv));
-              *reinterpret_cast<uint4*>(orow + h * 32 + x) = v;
+              *reinterpret_cast<uint4*>(orow + x) = v;
             }
+            if constexpr (HO > 32) {
+#pragma unroll
+              for (int x = 0; x < 16; x += 8) {
+                uint4 v = make_uint4(pack2(__uint_as_float(r2[x]) * inv, __uint_as_float(r2[x + 1]) * inv),
+                                     pack2(__uint_as_float(r2[x + 2]) * inv, __uint_as_float(r2[x + 3]) * inv),
+                                     pack2(__uint_as_float(r2[x + 4]) * inv, __uint_as_float(r2[x + 5]) * inv),
+                                     pack2(__uint_as_float(r2[x + 6]) * inv, __uint_as_float(r2[x + 7]) * inv));
+                *reinterpret_cast<uint4*>(orow + 32 + x) = v;
+              }
+            }
+            if (hf == 0) LSE[(int64_t)bh * Tn + i] = (m_run + log2f(l_tot)) * 0.69314718055994531f;
           }
         }
-        if (i < Tn) LSE[(int64_t)bh * Tn + i] = (m_run + log2f(l_run)) * 0.69314718055994531f;
       }
     }
   }
@@ -469,7 +532,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   tc::tc_fence_before();
   __syncthreads();
   tc::tc_fence_after();
-  if (warp == 9) tc::tmem_dealloc(tmem, TM_COLS);
+  if (warp == MMA_WARP) tc::tmem_dealloc(tmem, TM_COLS);
 }
 
 // cuTensorMapEncodeTiled is a driver-API function; it is resolved at run time

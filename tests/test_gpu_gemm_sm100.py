@@ -159,3 +159,32 @@ def test_large_shapes_match_cublas():
     for n in (6144, 32000):
         w = rn(n, 768, scale=0.05, seed=31)
         assert rel(G.mm_tn(x, w), x @ w.t()) < 4e-3
+
+
+@pytest.mark.parametrize("N", [64, 72, 136, 200])
+def test_two_epilogue_warp_sets_uneven_steps(N):
+    """SiLU' and SwiGLU-backward epilogues run two warp sets taking alternate
+    64-column steps; tiles with one step (the second set idle) or an odd step
+    count must still release the accumulator and write every column (the SiLU
+    forward epilogue, one set, on the same uneven shapes)."""
+    G = _g()
+    M, K = 1000, 256
+    x, w = rn(M, K, seed=40), rn(N, K, scale=0.05, seed=41)
+    z, a = G.mm_act(x, w, "silu")
+    z_ref = x.float() @ w.float().t()
+    assert rel(z, z_ref) < 4e-3 and rel(a, F.silu(z_ref)) < 8e-3
+    dy, w2 = rn(M, K, seed=42), rn(K, N, scale=0.05, seed=43)
+    dz = G.mm_act_grad(dy, w2, z, "silu")
+    zz = z.float()
+    sz = torch.sigmoid(zz)
+    assert rel(dz, (dy.float() @ w2.float()) * sz * (1 + zz * (1 - sz))) < 8e-3
+    if N % 8 == 0:
+        wu = rn(N, K, scale=0.05, seed=44)
+        gu, _ = G.swiglu_fwd(x, torch.cat([w, wu], 0)) if N % 32 == 0 else (None, None)
+        if gu is not None:
+            dgu = G.swiglu_dgrad(dy, w2, gu)
+            dh = dy.float() @ w2.float()
+            g, u = gu[:, :N].float(), gu[:, N:].float()
+            s = torch.sigmoid(g)
+            assert rel(dgu[:, :N], dh * u * s * (1 + g * (1 - s))) < 8e-3
+            assert rel(dgu[:, N:], dh * g * s) < 8e-3

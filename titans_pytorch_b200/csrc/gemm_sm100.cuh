@@ -20,12 +20,15 @@
 // leader's "full" barrier (cta_group::2 TMA form); MMA completion is
 // multicast by tcgen05.commit to both CTAs' "empty" / "acc_full" barriers.
 //
-// Warp roles per CTA (192 threads, one CTA per SM, persistent):
+// Warp roles per CTA (192 threads, or 320 for the epilogue-heavy modes; one
+// CTA per SM, persistent):
 //   warp 0      TMA producer (both CTAs)
 //   warp 1      TMEM allocator (both CTAs, collectively); MMA issuer (leader)
 //   warps 2-5   epilogue: thread = accumulator row (TMEM lane); two TMEM
 //               accumulators of BN columns, so the epilogue of one tile
 //               overlaps the next tile's main loop
+//   warps 6-9   (SiLU' and SwiGLU-backward epilogues) a second set over the
+//               same rows, taking every other column step
 //
 // Epilogue data path.  Each epilogue warp owns 32 accumulator rows and works
 // in 32 x 32 blocks: operands the epilogue reads (residual, saved
@@ -123,15 +126,34 @@ struct Maps {
   CUtensorMap a, b, c, c2, r, r2, ws;
 };
 
-template <int BN, int CG>
+// Epilogue warp sets.  The input-gradient epilogues that read saved
+// activations and compute a sigmoid and several products per output (SiLU'
+// product, SwiGLU backward) outlast the short main loop of their K =
+// model-width GEMMs; they run two sets of four epilogue warps over the same
+// accumulator rows (TMEM lane quarters), each set taking every other 64-column
+// step, and the main loop keeps three stages instead of five.  Measured on the
+// MAG shapes (32768 x 3072, K = 768): SiLU' 0.195 -> 0.172 ms, SwiGLU
+// backward 0.381 -> 0.353 ms; the SiLU forward epilogue (no input) was slower
+// with the shallower main loop (0.150 -> 0.189 ms) and keeps one set.
+template <int MODE>
+constexpr int epi_sets() {
+  return (MODE == SWIGLU_BWD || MODE == ACT_GRAD) ? 2 : 1;
+}
+template <int MODE>
+constexpr int nthreads() {
+  return 64 + 128 * epi_sets<MODE>();
+}
+
+template <int BN, int CG, int ES = 1>
 struct Cfg {
   static constexpr int A_BYTES = HM * BK * 2;
   static constexpr int B_BYTES = (BN / CG) * BK * 2;  // this CTA's B rows
   static constexpr int STAGE = A_BYTES + B_BYTES;
-  static constexpr int NS = (160 * 1024) / STAGE;
+  static constexpr int NS = (ES == 1 ? 160 * 1024 : 96 * 1024) / STAGE;
   static constexpr int OFF_STG = NS * STAGE;
-  static constexpr int OFF_BAR = OFF_STG + 4 * STG_WARP;
-  static constexpr int SMEM = OFF_BAR + 512 + 1024;
+  static constexpr int OFF_BAR = OFF_STG + 4 * ES * STG_WARP;
+  static constexpr int SMEM = OFF_BAR + 1024 + 1024;
+  static_assert(NS >= 3, "main-loop stages");
 };
 
 // ------------------------------------------------------------------ PTX helpers
@@ -473,9 +495,10 @@ __device__ __forceinline__ void ld_row128(const uint8_t* blk, int r, uint32_t (&
 }
 
 template <bool A_MN, bool B_MN, int MODE, int BN, int CG>
-__global__ void __cluster_dims__(CG, 1, 1) __launch_bounds__(NTHREADS, 1)
+__global__ void __cluster_dims__(CG, 1, 1) __launch_bounds__(nthreads<MODE>(), 1)
     gemm2_kernel(const __grid_constant__ Maps mp, const Args p) {
-  using C = Cfg<BN, CG>;
+  constexpr int ES = epi_sets<MODE>();
+  using C = Cfg<BN, CG, ES>;
   constexpr int BMT = HM * CG;  // tile rows
   constexpr int NS = C::NS;
   extern __shared__ uint8_t smem_raw[];
@@ -485,7 +508,7 @@ __global__ void __cluster_dims__(CG, 1, 1) __launch_bounds__(NTHREADS, 1)
   uint64_t* bar_acc_full = bar_empty + NS;
   uint64_t* bar_acc_empty = bar_acc_full + 2;
   uint64_t* bar_ld = bar_acc_empty + 2;  // 8 per epilogue warp (one per staging slot)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_ld + 32);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_ld + 32 * ES);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -499,9 +522,9 @@ __global__ void __cluster_dims__(CG, 1, 1) __launch_bounds__(NTHREADS, 1)
     }
     for (int b = 0; b < 2; ++b) {
       tc::mbar_init(bar_acc_full + b, 1);
-      tc::mbar_init(bar_acc_empty + b, CG * 4);  // one arrival per epilogue warp of every CTA of the tile
+      tc::mbar_init(bar_acc_empty + b, CG * 4 * ES);  // one arrival per epilogue warp of every CTA of the tile
     }
-    for (int b = 0; b < 32; ++b) tc::mbar_init(bar_ld + b, 1);
+    for (int b = 0; b < 32 * ES; ++b) tc::mbar_init(bar_ld + b, 1);
     *abort_flag = 0;
     tc::mbar_fence_init();
   }
@@ -608,14 +631,16 @@ __global__ void __cluster_dims__(CG, 1, 1) __launch_bounds__(NTHREADS, 1)
       }
     }
   } else {
-    // ------------------------------------------------------------ epilogue (warps 2-5)
-    // Steps (32-column blocks) of this warp's tiles form one stream; the
+    // ------------------------------------------------------------ epilogue (warps 2-5, and 6-9 with ES = 2)
+    // Steps (column blocks) of this warp's tiles form one stream; the
     // staging buffer is a ring of NSLOT step slots, and the input blocks of
     // step k + NSLOT - 1 are requested right after step k's stores, across
-    // tile boundaries, so load latency hides behind NSLOT - 1 steps.
+    // tile boundaries, so load latency hides behind NSLOT - 1 steps.  With two
+    // warp sets, set s takes steps s, s + 2, ... of every tile.
     constexpr int SLOT = slot_bytes<MODE>();
     constexpr int NSLOT = STG_WARP / SLOT;
     const int e = warp - EPI_WARP0;
+    const int set = e >> 2;
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     uint8_t* stg = smem + C::OFF_STG + e * STG_WARP;
     uint64_t* bl = bar_ld + 8 * e;
@@ -623,18 +648,25 @@ __global__ void __cluster_dims__(CG, 1, 1) __launch_bounds__(NTHREADS, 1)
     const uint32_t acc_empty0 = CG == 2 ? mapa(tc::smem_addr(bar_acc_empty), 0) : tc::smem_addr(bar_acc_empty);
     const float scale = p.scale;
     const int ffn_f = p.ffn_f;
-    // prefetch cursor (inputs only): next (item, step) whose inputs are requested
-    int pf_item = cid, pf_c = 0, pf_k = 0;
-    auto prefetch_until = [&](int upto) {  // lane 0: request inputs of every step < upto
+    // prefetch cursor (inputs only): next (item, step) of this warp whose inputs are requested
+    int pf_item = cid, pf_c = set, pf_k = 0;
+    auto prefetch_until = [&](int upto) {  // lane 0: request inputs of every own step < upto
       while (pf_k < upto && pf_item < p.items) {
         int pmt, pnt, psp;
         tile_of(p, pf_item, pmt, pnt, psp);
+        const int ns = step_count<MODE, BN>(p, pnt);
+        if (pf_c >= ns) {  // no (further) step of this warp in the tile
+          pf_c = set;
+          pf_item += ncl;
+          continue;
+        }
         const int prow0 = pmt * BMT + (int)rank * HM + q * 32;
         const int slot = pf_k % NSLOT;
         issue_in<MODE>(mp, ffn_f, stg + slot * SLOT, step_col<MODE, BN>(pnt, pf_c), prow0, bl + slot);
         ++pf_k;
-        if (++pf_c == step_count<MODE, BN>(p, pnt)) {
-          pf_c = 0;
+        pf_c += ES;
+        if (pf_c >= ns) {
+          pf_c = set;
           pf_item += ncl;
         }
       }
@@ -654,7 +686,12 @@ __global__ void __cluster_dims__(CG, 1, 1) __launch_bounds__(NTHREADS, 1)
       tc::tc_fence_after();
       const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + buf * BN;
       const int wrow = (item * CG + (int)rank) * HM + q * 32;  // PARTIAL: workspace rows
-      for (int c = 0; c < nsteps; ++c, ++step) {
+      if (set >= nsteps) {  // no step of this warp in the tile: release the accumulator at once
+        tc::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(acc_empty0 + buf * 8);
+      }
+      for (int c = set; c < nsteps; c += ES, ++step) {
         const int slot = step % NSLOT;
         uint8_t* sb = stg + slot * SLOT;
         const int n = step_col<MODE, BN>(nt, c);
@@ -676,7 +713,7 @@ __global__ void __cluster_dims__(CG, 1, 1) __launch_bounds__(NTHREADS, 1)
           tmem_row32(tbase + c * 32, *reinterpret_cast<float(*)[32]>(&v[0]));
         }
         if constexpr (MODE == SWIGLU) tmem_row32(tbase + BN / 2 + c * 32, u);
-        if (c == nsteps - 1) {  // accumulator drained: the MMA may reuse it
+        if (c + ES >= nsteps) {  // this warp's last read of the accumulator: the MMA may reuse it
           tc::tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive_cluster(acc_empty0 + buf * 8);
@@ -820,13 +857,13 @@ void launch_gemm2(const Maps& mp, const Args& a, cudaStream_t st);
 template <bool A_MN, bool B_MN, int MODE, int BN, int CG>
 void launch_gemm2_impl(const Maps& mp, const Args& a, cudaStream_t st) {
   static int ncl_max = -1;
-  using C = Cfg<BN, CG>;
+  using C = Cfg<BN, CG, epi_sets<MODE>()>;
   auto kern = gemm2_kernel<A_MN, B_MN, MODE, BN, CG>;
   if (ncl_max < 0) {
     C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(CG * (num_sms() / CG));
-    cfg.blockDim = dim3(NTHREADS);
+    cfg.blockDim = dim3(nthreads<MODE>());
     cfg.dynamicSmemBytes = C::SMEM;
     int c = 0;
     if (cudaOccupancyMaxActiveClusters(&c, kern, &cfg) != cudaSuccess || c <= 0) {
@@ -838,7 +875,7 @@ void launch_gemm2_impl(const Maps& mp, const Args& a, cudaStream_t st) {
   const int ncl = std::min(a.items, ncl_max);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(CG * ncl);
-  cfg.blockDim = dim3(NTHREADS);
+  cfg.blockDim = dim3(nthreads<MODE>());
   cfg.dynamicSmemBytes = C::SMEM;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];

@@ -196,3 +196,27 @@ def test_forward_and_memory_update_repeat_bitwise(kind):
     for a, b in zip(s1, s2):
         for x, y in zip(a.weights + a.momentum, b.weights + b.momentum):
             assert torch.equal(x, y)
+
+
+@pytest.mark.parametrize("kind", ["mac", "mag"])
+def test_side_stream_weight_grads_match_main_stream(kind):
+    """Small weight-gradient GEMMs on the side stream (MAC's per-segment shapes)
+    give the training result of the single-stream backward."""
+    from titans_pytorch_b200.train.trainer import Trainer, TrainStepConfig
+
+    fields = dict(dim=128, num_heads=2, num_layers=2, vocab_size=256, window_size=32, chunk_size=64,
+                  num_persistent_tokens=4, dropout=0.0, max_seq_len=256)
+    torch.manual_seed(0)
+    base = T.create_model(kind, T.TitansConfig(**fields))
+    runs = []
+    for side in (True, False):
+        tr = Trainer(copy.deepcopy(base), TrainStepConfig(lr=1e-3), device="cuda")
+        tr._side_wgrad = side
+        g = torch.Generator().manual_seed(1)
+        for _ in range(2):
+            ids = torch.randint(0, 256, (2, 193), generator=g)
+            tr.train_step({"input_ids": ids[:, :-1], "labels": ids[:, 1:]})
+        torch.cuda.synchronize()
+        runs.append({k: v.float().clone() for k, v in tr.model.state_dict().items()})
+    for k in runs[0]:
+        torch.testing.assert_close(runs[0][k], runs[1][k], atol=5e-3, rtol=1e-2, msg=k)

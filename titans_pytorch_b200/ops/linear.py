@@ -36,7 +36,13 @@ import torch.nn.functional as F
 from . import gemm as G
 from ._ext import want_kernels
 
-_STATE = {"inplace": False, "prefetch": None}
+_STATE = {"inplace": False, "prefetch": None, "side": None, "side_used": False}
+_SIDE_STREAMS: dict[int, "torch.cuda.Stream"] = {}
+
+# A weight gradient this small (few output tiles, a short reduction over the
+# tokens) leaves most of the GPU idle on its own: MAC's per-segment GEMMs.
+SIDE_MAX_TOKENS = 4096
+SIDE_MAX_TILES = 36  # 256 x 256 output tiles: half of the 74 CTA pairs
 
 
 def set_prefetch(fn) -> None:
@@ -45,13 +51,39 @@ def set_prefetch(fn) -> None:
 
 
 @contextlib.contextmanager
-def accumulate_weight_grads(enabled: bool = True):
-    prev = _STATE["inplace"]
+def accumulate_weight_grads(enabled: bool = True, side_stream: bool = False):
+    """In-place weight gradients (see the module docstring).  ``side_stream``
+    (CUDA): weight-gradient GEMMs too small to fill the GPU (at most
+    ``SIDE_MAX_TOKENS`` tokens and ``SIDE_MAX_TILES`` output tiles) run on a
+    second stream, so they fill the SMs that the backward's critical path
+    (input gradients) leaves idle; the current stream waits for that stream
+    when the context exits, before anything reads the gradients.  Callers whose
+    code reads ``.grad`` inside the backward (reductions during the backward)
+    must not ask for it."""
+    prev = (_STATE["inplace"], _STATE["side"], _STATE["side_used"])
     _STATE["inplace"] = enabled
+    side = None
+    main = None
+    if enabled and side_stream and torch.cuda.is_available():
+        main = torch.cuda.current_stream()
+        key = main.device.index
+        side = _SIDE_STREAMS.get(key)
+        if side is None:
+            side = _SIDE_STREAMS[key] = torch.cuda.Stream(main.device)
+    _STATE["side"], _STATE["side_used"] = side, False
     try:
         yield
     finally:
-        _STATE["inplace"] = prev
+        if side is not None and _STATE["side_used"]:
+            main.wait_stream(side)  # every weight gradient is complete from here on
+        _STATE["inplace"], _STATE["side"], _STATE["side_used"] = prev
+
+
+def _side_ok(dy2: torch.Tensor, target: torch.Tensor) -> bool:
+    if _STATE["side"] is None or not dy2.is_cuda or dy2.shape[0] > SIDE_MAX_TOKENS:
+        return False
+    tiles = ((target.shape[0] + 255) // 256) * ((target.shape[1] + 255) // 256)
+    return tiles <= SIDE_MAX_TILES
 
 
 def inplace_grads_enabled() -> bool:
@@ -142,7 +174,15 @@ def weight_grads(weights, dy2: torch.Tensor, x2: torch.Tensor, kern: bool, need)
     Nones), else returned for autograd."""
     target = grad_target(weights) if (_STATE["inplace"] and all(need)) else None
     if target is not None:
-        if kern and G.operand_ok(target):
+        if kern and G.operand_ok(target) and _side_ok(dy2, target):
+            side = _STATE["side"]
+            side.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(side):
+                G.mm_wgrad(dy2, x2, out=target, accumulate=True)
+            dy2.record_stream(side)  # the allocator must not reuse them before the side stream has read them
+            x2.record_stream(side)
+            _STATE["side_used"] = True
+        elif kern and G.operand_ok(target):
             G.mm_wgrad(dy2, x2, out=target, accumulate=True)
         else:
             target.addmm_(dy2.t(), x2.to(dy2.dtype))

@@ -278,6 +278,8 @@ class FSDPAdamW(FusedAdamW):
         self.last_grad_norm = self.norm_out
         self._tab_key = None
         self.graph_safe = fused
+        # per-call / per-block reductions read the gradients inside the backward
+        self.reduces_during_backward = self.reshard or (self.overlap and fused) or not self.replicate_units
 
         # ---------------------------------------------------------- reduction tables
         w, me = self.world, self.rank

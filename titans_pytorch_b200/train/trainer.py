@@ -78,6 +78,9 @@ class Trainer:
         self.global_step = 0
         self._micro = 0
         self.optimizer.zero_grad()
+        # small weight gradients on a second stream, unless the engine reads the
+        # gradients during the backward (reductions of finished blocks)
+        self._side_wgrad = self.device.type == "cuda" and not getattr(self.optimizer, "reduces_during_backward", False)
         self._graph = None
         self._eager_graph_steps = 0
         if self.cfg.cuda_graph:
@@ -110,7 +113,7 @@ class Trainer:
         prep = getattr(self.optimizer, "prepare_backward", None)
         if prep is not None:  # engines that reduce during the backward: is this the step's last one?
             prep((self._micro + 1) % accum == 0)
-        with accumulate_weight_grads():
+        with accumulate_weight_grads(side_stream=self._side_wgrad):
             (loss / accum if accum > 1 else loss).backward()
         self._micro += 1
         if self._micro % accum == 0:
@@ -138,7 +141,7 @@ class Trainer:
                 ids = self._to_device(batch["input_ids"])
                 labels = self._to_device(batch["labels"])
                 loss = self.loss_fn(ids, labels)
-                with accumulate_weight_grads():
+                with accumulate_weight_grads(side_stream=self._side_wgrad):
                     loss.backward()
                 self.optimizer_step()
             cur.wait_stream(side)
@@ -165,7 +168,7 @@ class Trainer:
         saved_count = opt.step_count
         with torch.cuda.graph(g):
             loss = self.loss_fn(self._static_ids, self._static_labels)
-            with accumulate_weight_grads():
+            with accumulate_weight_grads(side_stream=self._side_wgrad):
                 loss.backward()
             if self.engine is not None:
                 self.engine.reduce_gradients(opt)

@@ -86,6 +86,7 @@ def main(argv=None) -> None:
     gw3, gwd = torch.zeros(3 * D, D, device=dev, dtype=torch.bfloat16), torch.zeros(D, Fd, device=dev,
                                                                                    dtype=torch.bfloat16)
     out3 = torch.empty(T, 3 * D, device=dev, dtype=torch.bfloat16)
+    gu_saved = rn(T, 2 * Fd)  # the [g | u] buffer the SwiGLU forward saves
     cases = {
         # name: (flops, ours, cublas)
         "qkv_fwd": (2 * T * D * 3 * D, lambda: G.mm_tn(x, w3, out=out3), lambda: torch.matmul(x, w3.t(), out=out3)),
@@ -106,6 +107,8 @@ def main(argv=None) -> None:
                          lambda: E.act_grad_mul(torch.matmul(dyd, wd), hf, "silu")),
         "mem_err": (2 * T * Fd * D, lambda: G.mm_err(hf, wd, dyd, 1e-3),
                     lambda: E.scaled_err(torch.matmul(hf, wd.t()), dyd, 1e-3)),
+        "ffn_swiglu_bwd": (2 * T * D * Fd, lambda: G.swiglu_dgrad(dyd, wd, gu_saved),
+                           lambda: E.swiglu_bwd(torch.matmul(dyd, wd), gu_saved)),
         "ffn_down_resid": (2 * T * Fd * D, lambda: G.mm_tn(hf, wd, mode="resid", r=dyd),
                            lambda: torch.matmul(hf, wd.t()).add_(dyd)),
         "head_fwd": (2 * T * D * V, lambda: G.mm_tn(x, wh), lambda: torch.matmul(x, wh.t())),

@@ -165,6 +165,8 @@ def test_cli_pretrain_infer_eval_pretokenize(tmp_path, capsys):
     final = ck / "final_model.pt"
     assert final.exists()
     inference.main(["--checkpoint", str(final), "--prompt", "the", "--max-tokens", "5", "--device", "cpu"])
+    inference.main(["--checkpoint", str(final), "--prompt", "the", "--max-tokens", "5", "--device", "cpu",
+                    "--decoder", "incremental", "--quantize", "int8"])
     eval_perplexity.main(["--checkpoint", str(final), "--data", str(text), "--max-length", "64", "--stride",
                           "32", "--device", "cpu", "--max-tokens", "300"])
     eval_perplexity.main(["--checkpoint", str(final), "--data", str(text), "--use-memory", "--chunk-size", "32",

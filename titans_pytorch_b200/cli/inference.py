@@ -29,6 +29,9 @@ def build_parser() -> argparse.ArgumentParser:
     a("--interactive", action="store_true")
     a("--stream", action="store_true")
     a("--quantize", choices=["int8", "int4", "fp16"], default=None)
+    a("--decoder", choices=["recurrence", "incremental"], default="recurrence",
+      help="recurrence: re-run the last chunk per token (the reference's decoding); incremental: one "
+           "token per step over a sliding-window KV cache with the memory state carried (MAG / MAL / LMM)")
     a("--device", default=None)
     a("--seed", type=int, default=0)
     return p
@@ -40,6 +43,15 @@ def run_prompt(model, tok, prompt: str, args, out=sys.stdout) -> str:
     x = torch.tensor([ids], dtype=torch.long, device=dev)
     kw = dict(temperature=args.temperature, top_k=args.top_k, top_p=args.top_p,
               repetition_penalty=args.repetition_penalty, eos_token_id=getattr(tok, "eos_token_id", None))
+    if getattr(args, "decoder", "recurrence") == "incremental" and getattr(model, "model_type", "") != "mac":
+        from ..inference.decode import generate_incremental
+
+        ids_, _ = generate_incremental(model, x, args.max_tokens, **kw)
+        text = tok.decode(ids_[0, x.shape[1]:].tolist())
+        out.write(prompt + text + "\n")
+        return text
+    if getattr(args, "decoder", "recurrence") == "incremental":
+        print("note: MAC decodes with the recurrence (no incremental decoder for it)", file=sys.stderr)
     if args.stream:
         text, n0 = "", x.shape[1]
         for ids_, _ in generate(model, x, args.max_tokens, stream=True, **kw):

@@ -5,7 +5,8 @@
   uninterrupted run's final weights (data position, optimizer shards,
   scheduler and RNG restored);
 * ``--eval-every`` evaluates a held-out set, logs ``val/loss`` and keeps
-  ``best_model.pt``; fp16 is refused; ``--torch-compile`` on CPU runs eagerly.
+  ``best_model.pt``; fp16 is refused; ``--torch-compile`` on CPU runs eagerly;
+* ``--parallel cp`` trains with every sequence split over two gloo ranks.
 """
 
 from __future__ import annotations
@@ -50,6 +51,20 @@ def test_distributed_resume_with_optimizer_shards(tmp_path):
     wa, wb = _weights(a / "final_model.pt"), _weights(b / "final_model.pt")
     for k in wa:
         torch.testing.assert_close(wb[k], wa[k], rtol=1e-5, atol=1e-6, msg=k)
+
+
+def test_context_parallel_cli(tmp_path):
+    """--parallel cp: two gloo ranks each train on half of every sequence (with evaluation)."""
+    ck, mf = tmp_path / "ck", tmp_path / "m.jsonl"
+    argv = COMMON + ["--parallel", "cp", "--max-steps", "3", "--eval-every", "2", "--eval-batches", "2",
+                     "--save-every", "0", "--checkpoint-dir", str(ck), "--metrics-file", str(mf),
+                     "--heartbeat-timeout", "30", "--dist-timeout", "60"]
+    run_workers(_rank_main, 2, (argv,), timeout=240)
+    lines = [json.loads(x) for x in mf.read_text().splitlines()]
+    losses = [x["train/loss"] for x in lines if "train/loss" in x]
+    assert losses and all(0 < v < 20 for v in losses)
+    assert any("val/loss" in x for x in lines)
+    assert (ck / "final_model.pt").exists()
 
 
 def test_eval_loop_and_best_model(tmp_path):

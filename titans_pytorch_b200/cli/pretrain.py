@@ -84,9 +84,10 @@ def build_parser() -> argparse.ArgumentParser:
     a("--weight-decay", type=float, default=0.1)
     a("--grad-clip", type=float, default=1.0)
     a("--warmup-ratio", type=float, default=0.03)
-    a("--parallel", choices=["dp", "fsdp"], default="dp",
+    a("--parallel", choices=["dp", "fsdp", "cp"], default="dp",
       help="under torchrun: dp = replicated weights with the optimizer state sharded; fsdp = parameters "
-           "sharded per block, all-gathered in the forward")
+           "sharded per block, all-gathered in the forward; cp = context parallel (MAG/MAL/LMM): every "
+           "sequence split over the ranks, halos exchanged, memory updates averaged")
     a("--mixed-precision", choices=["none", "fp16", "bf16"], default="bf16",
       help="bf16 (default) or none (fp32); fp16 is rejected: the kernels compute in bf16")
     a("--checkpoint-dir", type=str, default="checkpoints")
@@ -189,28 +190,43 @@ def run(args) -> dict:
         fields.update(TitansConfig.from_file(args.config).to_dict())
     cfg = TitansConfig(**fields)
     model = create_model(args.model, cfg)
+    cp = None
+    if args.parallel == "cp" and world > 1:
+        from ..parallel.context import enable_context_parallel
+
+        cp = enable_context_parallel(model)
+        if args.seq_len % world:
+            raise SystemExit(f"--parallel cp: --seq-len {args.seq_len} must be divisible by {world} ranks")
     if args.gradient_checkpointing:
         enable_gradient_checkpointing(model)
     ds, eval_ds = split_eval(args, build_dataset(args, cfg.vocab_size), cfg.vocab_size)
-    sampler = DistributedSampler(ds, world, rank, shuffle=True, seed=args.seed) if (
+    # context parallel: every rank reads the same whole sequences and keeps its shard of them
+    dworld, drank = (1, 0) if cp is not None else (world, rank)
+    sampler = DistributedSampler(ds, dworld, drank, shuffle=True, seed=args.seed) if (
         world > 1 and hasattr(ds, "__len__")) else None
     loader = DataLoader(ds, batch_size=args.batch_size, shuffle=(sampler is None and hasattr(ds, "__len__")),
                         sampler=sampler, num_workers=args.num_workers, pin_memory=device.type == "cuda",
                         drop_last=True)
     eval_loader = None
     if eval_ds is not None:
-        es = DistributedSampler(eval_ds, world, rank, shuffle=False) if world > 1 else None
+        es = DistributedSampler(eval_ds, dworld, drank, shuffle=False) if world > 1 else None
         eval_loader = DataLoader(eval_ds, batch_size=args.batch_size, sampler=es, shuffle=False, drop_last=True,
                                  num_workers=0, pin_memory=device.type == "cuda")
+    if cp is not None:
+        from ..parallel.context import ShardedLoader
+
+        loader = ShardedLoader(loader, cp)
+        eval_loader = ShardedLoader(eval_loader, cp) if eval_loader is not None else None
     steps_per_epoch = len(loader) // args.gradient_accumulation_steps if hasattr(ds, "__len__") else 10 ** 9
     total = args.max_steps if args.max_steps > 0 else steps_per_epoch * args.epochs
     dtype = {"bf16": torch.bfloat16, "none": torch.float32}[args.mixed_precision]
     graph = False
     if args.torch_compile:
-        graph = device.type == "cuda" and args.gradient_accumulation_steps == 1
+        graph = device.type == "cuda" and args.gradient_accumulation_steps == 1 and cp is None
         log.info("--torch-compile (%s): %s", args.compile_mode,
                  "whole-step CUDA-graph capture and replay" if graph else
-                 "no CUDA graph (needs a CUDA device and no gradient accumulation); running eagerly")
+                 "no CUDA graph (needs a CUDA device, no gradient accumulation and no context "
+                 "parallelism); running eagerly")
     tr = Trainer(model, TrainStepConfig(lr=args.lr, weight_decay=args.weight_decay, grad_clip=args.grad_clip,
                                         warmup_steps=int(total * args.warmup_ratio), total_steps=total,
                                         gradient_accumulation_steps=args.gradient_accumulation_steps, dtype=dtype,
@@ -249,7 +265,7 @@ def run(args) -> dict:
                                  model_type=args.model, tokenizer_name=args.tokenizer, train_config=vars(args),
                                  data_position=position)
 
-    tokens_per_step = args.batch_size * args.seq_len * world * args.gradient_accumulation_steps
+    tokens_per_step = args.batch_size * args.seq_len * dworld * args.gradient_accumulation_steps
     t_last, s_last = time.perf_counter(), tr.global_step
     last = {}
     done = False

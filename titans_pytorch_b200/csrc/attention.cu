@@ -132,7 +132,7 @@ __device__ __forceinline__ void rope8(float (&v)[8], const float* inv_freq, int 
 template <typename T>
 __global__ void pack_kernel(const T* __restrict__ qkv, int64_t sb, int64_t sr, const T* __restrict__ pkv, int Bp,
                             const float* __restrict__ inv_freq, bf16* __restrict__ Q, bf16* __restrict__ K,
-                            bf16* __restrict__ V, int B, int Tn, int P, int H, int HD) {
+                            bf16* __restrict__ V, int B, int Tn, int P, int H, int HD, int pos0) {
   const int D = H * HD;
   const int cpr = HD / 8;
   const int64_t total = (int64_t)B * (P + Tn) * H * cpr;
@@ -156,11 +156,12 @@ __global__ void pack_kernel(const T* __restrict__ qkv, int64_t sb, int64_t sr, c
       load8<T>(row + col, q);
       load8<T>(row + D + col, k);
       load8<T>(row + 2 * D + col, v);
-      // the query at main position i = j - P has rope position P + i = j
-      rope8(q, inv_freq, c * 4, (float)j, 1.f);
+      // the query at main position i = j - P has rope position P + i + pos0 = j + pos0
+      // (pos0: the main rows' offset in a longer sequence, e.g. a context-parallel shard)
+      rope8(q, inv_freq, c * 4, (float)(j + pos0), 1.f);
       store8<bf16>(Q + (((int64_t)b * H + h) * Tn + (j - P)) * HD + c * 8, q);
     }
-    rope8(k, inv_freq, c * 4, (float)j, 1.f);
+    rope8(k, inv_freq, c * 4, (float)(j < P ? j : j + pos0), 1.f);
     store8<bf16>(K + kidx, k);
     store8<bf16>(V + kidx, v);
   }
@@ -171,7 +172,7 @@ __global__ void pack_kernel(const T* __restrict__ qkv, int64_t sb, int64_t sr, c
 template <typename T>
 __global__ void unpack_kernel(const float* __restrict__ dQa, const float* __restrict__ dKa,
                               const float* __restrict__ dVa, const float* __restrict__ inv_freq, T* __restrict__ dqkv,
-                              T* __restrict__ dpkv, int Bp, int B, int Tn, int P, int H, int HD) {
+                              T* __restrict__ dpkv, int Bp, int B, int Tn, int P, int H, int HD, int pos0) {
   const int D = H * HD;
   const int cpr = HD / 8;
   const int64_t total_main = (int64_t)B * Tn * H * cpr;
@@ -192,8 +193,8 @@ __global__ void unpack_kernel(const float* __restrict__ dQa, const float* __rest
       load8f(dKa + (bh * (P + Tn) + j) * HD + c * 8, dk);
       load8f(dVa + (bh * (P + Tn) + j) * HD + c * 8, dv);
       // inverse rotation: R(-a) applied to the gradient of the rotated vector
-      rope8(dq, inv_freq, c * 4, (float)j, -1.f);
-      rope8(dk, inv_freq, c * 4, (float)j, -1.f);
+      rope8(dq, inv_freq, c * 4, (float)(j + pos0), -1.f);
+      rope8(dk, inv_freq, c * 4, (float)(j + pos0), -1.f);
       T* row = dqkv + ((int64_t)b * Tn + t) * 3 * D + h * HD + c * 8;
       store8<T>(row, dq);
       store8<T>(row + D, dk);
@@ -714,8 +715,9 @@ using attn::bf16;
 
 // qkv [B, T, 3D] (last dim contiguous); pkv [Bp, P, 2D] or undefined.
 // returns {Q, K, V} packed bf16 with RoPE applied.
+// pos0: rope position offset of the main rows (prefix rows keep positions 0..P-1)
 std::vector<at::Tensor> attn_pack(const at::Tensor& qkv, const c10::optional<at::Tensor>& pkv_opt, int64_t H,
-                                  const c10::optional<at::Tensor>& inv_freq) {
+                                  const c10::optional<at::Tensor>& inv_freq, int64_t pos0) {
   TB_CHECK_CUDA(qkv);
   TB_CHECK_LASTDIM(qkv);
   const at::cuda::CUDAGuard g(qkv.device());
@@ -744,7 +746,7 @@ std::vector<at::Tensor> attn_pack(const at::Tensor& qkv, const c10::optional<at:
     attn::pack_kernel<scalar_t><<<blocks, 256, 0, stream()>>>(
         (const scalar_t*)qkv.data_ptr(), qkv.stride(0), qkv.stride(1),
         P ? (const scalar_t*)pkv.data_ptr() : nullptr, Bp, inv.defined() ? inv.data_ptr<float>() : nullptr,
-        (bf16*)Q.data_ptr(), (bf16*)K.data_ptr(), (bf16*)V.data_ptr(), B, Tn, P, (int)H, HD);
+        (bf16*)Q.data_ptr(), (bf16*)K.data_ptr(), (bf16*)V.data_ptr(), B, Tn, P, (int)H, HD, (int)pos0);
   });
   check_launch("attn_pack");
   return {Q, K, V};
@@ -824,7 +826,8 @@ std::vector<at::Tensor> attn_bwd_packed(const at::Tensor& dO_in, const at::Tenso
 
 // returns {dqkv [B, T, 3D], dpkv [Bp, P, 2D] (empty when P == 0)}
 std::vector<at::Tensor> attn_unpack(const at::Tensor& dQa, const at::Tensor& dKa, const at::Tensor& dVa,
-                                    const c10::optional<at::Tensor>& inv_freq, int64_t Bp, at::ScalarType dtype) {
+                                    const c10::optional<at::Tensor>& inv_freq, int64_t Bp, at::ScalarType dtype,
+                                    int64_t pos0) {
   const at::cuda::CUDAGuard g(dQa.device());
   const int B = dQa.size(0), H = dQa.size(1), Tn = dQa.size(2), HD = dQa.size(3);
   const int P = dKa.size(2) - Tn;
@@ -840,7 +843,7 @@ std::vector<at::Tensor> attn_unpack(const at::Tensor& dQa, const at::Tensor& dKa
     attn::unpack_kernel<scalar_t><<<blocks, 256, 0, stream()>>>(
         dQa.data_ptr<float>(), dKa.data_ptr<float>(), dVa.data_ptr<float>(),
         inv.defined() ? inv.data_ptr<float>() : nullptr, (scalar_t*)dqkv.data_ptr(),
-        P ? (scalar_t*)dpkv.data_ptr() : nullptr, (int)Bp, B, Tn, P, H, HD);
+        P ? (scalar_t*)dpkv.data_ptr() : nullptr, (int)Bp, B, Tn, P, H, HD, (int)pos0);
   });
   check_launch("attn_unpack");
   return {dqkv, dpkv};

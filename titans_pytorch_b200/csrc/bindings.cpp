@@ -42,14 +42,15 @@ void adamw_hyper_step(at::Tensor& hyper, double base_lr, double beta1, double be
                       double min_ratio, bool use_schedule);
 // attention.cu
 std::vector<at::Tensor> attn_pack(const at::Tensor& qkv, const c10::optional<at::Tensor>& pkv, int64_t H,
-                                  const c10::optional<at::Tensor>& inv_freq);
+                                  const c10::optional<at::Tensor>& inv_freq, int64_t pos0);
 std::vector<at::Tensor> attn_fwd_packed(const at::Tensor& Q, const at::Tensor& K, const at::Tensor& V, int64_t window,
                                         double scale);
 std::vector<at::Tensor> attn_bwd_packed(const at::Tensor& dO, const at::Tensor& Q, const at::Tensor& K,
                                         const at::Tensor& V, const at::Tensor& O, const at::Tensor& LSE,
                                         int64_t window, double scale);
 std::vector<at::Tensor> attn_unpack(const at::Tensor& dQa, const at::Tensor& dKa, const at::Tensor& dVa,
-                                    const c10::optional<at::Tensor>& inv_freq, int64_t Bp, at::ScalarType dtype);
+                                    const c10::optional<at::Tensor>& inv_freq, int64_t Bp, at::ScalarType dtype,
+                                    int64_t pos0);
 // attention_tc.cu
 std::vector<at::Tensor> attn_fwd_tc(const at::Tensor& Q, const at::Tensor& K, const at::Tensor& V, int64_t window,
                                     double scale);
@@ -125,10 +126,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         pybind11::arg("beta1"), pybind11::arg("beta2"), pybind11::arg("eps"), pybind11::arg("wd"),
         pybind11::arg("step"), pybind11::arg("hyper") = pybind11::none());
   m.def("adamw_hyper_step", &tb::adamw_hyper_step);
-  m.def("attn_pack", &tb::attn_pack);
+  m.def("attn_pack", &tb::attn_pack, py::arg("qkv"), py::arg("pkv"), py::arg("H"), py::arg("inv_freq"),
+        py::arg("pos0") = 0);
   m.def("attn_fwd_packed", &tb::attn_fwd_packed);
   m.def("attn_bwd_packed", &tb::attn_bwd_packed);
-  m.def("attn_unpack", &tb::attn_unpack);
+  m.def("attn_unpack", &tb::attn_unpack, py::arg("dQa"), py::arg("dKa"), py::arg("dVa"), py::arg("inv_freq"),
+        py::arg("Bp"), py::arg("dtype"), py::arg("pos0") = 0);
   m.def("attn_fwd_tc", &tb::attn_fwd_tc);
   m.def("attn_tc_supported", &tb::attn_tc_supported);
   m.def("attn_tc_fwd_supported", &tb::attn_tc_fwd_supported);

@@ -83,13 +83,17 @@ class _AttentionBase(nn.Module):
     # stacked projections below read adjacent weights in place, so nothing is cached.
     _wcache: dict | None = None
 
-    def _attend(self, qkv, pkv, window):
-        """qkv: [B, T, 3D]; pkv: [B or 1, P, 2D] or None -> [B, T, D] after proj_out."""
+    def _attend(self, qkv, pkv, window, context_rows: int = 0, pos_offset: int = 0):
+        """qkv: [B, T, 3D]; pkv: [B or 1, P, 2D] or None -> [B, T - context_rows, D] after proj_out."""
         o = window_attention(
             qkv, pkv, self.num_heads, window=window, scale=self.scale,
             inv_freq=None if self.rope is None else self.rope.inv_freq,
-            dropout_p=self.dropout.p, training=self.training, use_kernels=self.use_kernels)
-        return linear(o.reshape(*qkv.shape[:-1], self.dim), self.proj_out.weight, use_kernels=self.use_kernels)
+            dropout_p=self.dropout.p, training=self.training, use_kernels=self.use_kernels,
+            pos_offset=pos_offset)
+        o = o.reshape(*qkv.shape[:-1], self.dim)
+        if context_rows:
+            o = o[:, context_rows:].contiguous()
+        return linear(o, self.proj_out.weight, use_kernels=self.use_kernels)
 
     def _project(self, x: torch.Tensor, kv_only: bool = False) -> torch.Tensor:
         """x @ [Wq; Wk; Wv]^T (or [Wk; Wv] with ``kv_only``); weight gradients
@@ -107,12 +111,18 @@ class SlidingWindowAttention(_AttentionBase):
         self.window_size = config.window_size
 
     def forward(self, x: torch.Tensor, prefix: torch.Tensor | None = None,
-                seq_offset: int = 0) -> torch.Tensor:
+                seq_offset: int = 0, context_rows: int = 0, position_offset: int = 0) -> torch.Tensor:
         """``x`` [B, T, D], ``prefix`` [B, P, D] or None.
 
         ``seq_offset`` shifts every RoPE position by the same amount; rotary
         scores depend only on position differences, so the output does not
         change with it (the argument is kept for API compatibility).
+
+        Context parallelism: the first ``context_rows`` rows of ``x`` are the
+        previous shard's last rows (keys and values only; no output row), and
+        ``position_offset`` is the global token index of ``x``'s first row, so
+        the prefix keys keep positions ``0..P-1`` and the shard's rows get
+        their positions in the whole sequence.
         """
         del seq_offset
         qkv = self._project(x)
@@ -121,7 +131,7 @@ class SlidingWindowAttention(_AttentionBase):
             if prefix.stride(0) == 0:  # batch-broadcast persistent tokens: project once
                 prefix = prefix[:1]
             pkv = self._project(prefix, kv_only=True)
-        return self._attend(qkv, pkv, self.window_size)
+        return self._attend(qkv, pkv, self.window_size, context_rows, position_offset)
 
     # Mask helpers (same contract as the reference's, used by tests and debugging)
     def _create_sliding_window_mask(self, seq_len: int, device) -> torch.Tensor:

@@ -33,7 +33,7 @@ import torch.nn.functional as F
 from ..config import TitansConfig
 from ..ops.conv import conv_silu_norm
 from ..ops.memory import (activation, activation_fn, memory_grads_reference, memory_mlp, memory_step,
-                          mlp_forward_reference, mlp_kernel_ok)
+                          memory_step_sharded, mlp_forward_reference, mlp_kernel_ok)
 from ..ops.linear import linear
 from ..ops.memory_paper import head_blocks, memory_scan, memory_scan_reference
 
@@ -175,23 +175,40 @@ class NeuralLongTermMemory(nn.Module):
         g = (self.gate_decay[0], self.gate_lr[0], self.gate_momentum[0])
         return [m.weight for m in g], [m.bias for m in g]
 
-    def _queries(self, x: torch.Tensor) -> torch.Tensor:
+    # ContextShard while the owning model runs context-parallel (parallel.context)
+    cp = None
+
+    def _trim(self, x: torch.Tensor, rows: int) -> tuple[torch.Tensor, int]:
+        """Keep of the ``rows`` leading halo rows of ``x`` only the ``K - 1`` the
+        causal convolutions read."""
+        if rows == 0:
+            return x, 0
+        keep = min(rows, self.config.conv_kernel_size - 1 if self.use_conv else 0)
+        return x[:, rows - keep:], keep
+
+    @staticmethod
+    def _drop(t: torch.Tensor, rows: int) -> torch.Tensor:
+        return t[:, rows:].contiguous() if rows else t
+
+    def _queries(self, x: torch.Tensor, context_rows: int = 0) -> torch.Tensor:
+        x, r = self._trim(x, context_rows)
         wq, bq = self._conv("conv_q")
-        return conv_silu_norm(linear(x, self.proj_q.weight, use_kernels=self.use_kernels), wq, bq, True,
-                              self.use_kernels)
+        return self._drop(conv_silu_norm(linear(x, self.proj_q.weight, use_kernels=self.use_kernels), wq, bq,
+                                         True, self.use_kernels), r)
 
     # per-forward cache of derived weights, set by the owning model (see SegmentedAttention)
     _wcache: dict | None = None
 
     @torch.no_grad()
-    def _keys_values(self, x: torch.Tensor):
+    def _keys_values(self, x: torch.Tensor, context_rows: int = 0):
         D = self.dim
+        x, r = self._trim(x, context_rows)
         kv = linear(x, self.proj_k.weight, self.proj_v.weight, use_kernels=self.use_kernels)
         wk, bk = self._conv("conv_k")
         wv, bv = self._conv("conv_v")
         k = conv_silu_norm(kv[..., :D], wk, bk, True, self.use_kernels)
         v = conv_silu_norm(kv[..., D:], wv, bv, False, self.use_kernels)
-        return k, v
+        return self._drop(k, r), self._drop(v, r)
 
     def _apply_conv(self, k, v, q):
         """Causal depthwise convolution of k, v, q (no activation); API parity helper."""
@@ -305,23 +322,39 @@ class NeuralLongTermMemory(nn.Module):
         w = self.memory.get_weights()
         return MemoryState(weights=w, momentum=[torch.zeros_like(t) for t in w])
 
-    def _update(self, x: torch.Tensor, state: MemoryState) -> MemoryState:
-        """New state after one update with the tokens of ``x`` (no retrieval output)."""
+    def _update(self, x: torch.Tensor, state: MemoryState, context_rows: int = 0) -> MemoryState:
+        """New state after one update with the tokens of ``x`` (no retrieval output).
+
+        ``context_rows`` leading rows of ``x`` are a halo from the previous
+        sequence shard: read by the convolutions only.  Under context
+        parallelism the update averages its statistics over the shards.
+        """
         if self.paper:
             with torch.no_grad():
                 return self._paper_scan(x.detach(), state)[1]
-        k, v = self._keys_values(x)
+        k, v = self._keys_values(x, context_rows)
         gw, gb = self._gate_params()
-        new_w, new_m = memory_step(k, v, x.detach(), state.weights, state.momentum, gw, gb,
-                                   self.config.memory_lr, self.config.memory_momentum,
-                                   self.config.activation, self._linear_silu, self.use_kernels)
+        xs = x[:, context_rows:].detach()
+        if self.cp is not None and self.cp.active:
+            new_w, new_m = memory_step_sharded(k, v, xs, state.weights, state.momentum, gw, gb,
+                                               self.config.memory_lr, self.config.memory_momentum,
+                                               self.config.activation, self._linear_silu, self.use_kernels,
+                                               self.cp)
+        else:
+            new_w, new_m = memory_step(k, v, xs, state.weights, state.momentum, gw, gb,
+                                       self.config.memory_lr, self.config.memory_momentum,
+                                       self.config.activation, self._linear_silu, self.use_kernels)
         if self._freezes_mlp:
             self.memory.requires_grad_(False)
         return MemoryState(new_w, new_m).detach()
 
     def forward(self, x: torch.Tensor, state: MemoryState | None = None,
-                return_state: bool = True, update: bool = True):
+                return_state: bool = True, update: bool = True, context_rows: int = 0):
         """Retrieve with the incoming memory and update it with ``x``.
+
+        The first ``context_rows`` rows of ``x`` are a halo from the previous
+        sequence shard (context parallelism): they feed the convolutions and
+        produce no output row.
 
         Returns ``(proj_out(M_{t-1}(q)), new_state or None)``.  ``update=False``
         skips the (gradient-free) update and returns no state; activation
@@ -333,11 +366,13 @@ class NeuralLongTermMemory(nn.Module):
         elif not self.paper:
             self.memory.set_weights(state.weights)
         if self.paper:
+            if context_rows:
+                raise NotImplementedError("paper semantics has no context-parallel form")
             y, new_state = self._paper_scan(x, state)
             out = F.linear(y, self.proj_out.weight)
             return (out, new_state) if return_state else (out, None)
-        retrieved = self.memory(self._queries(x))
-        new_state = self._update(x, state) if update else None
+        retrieved = self.memory(self._queries(x, context_rows))
+        new_state = self._update(x, state, context_rows) if update else None
         out = linear(retrieved, self.proj_out.weight, use_kernels=self.use_kernels)
         return (out, new_state) if return_state else (out, None)
 

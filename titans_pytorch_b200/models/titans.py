@@ -34,6 +34,20 @@ def _norm(config: TitansConfig) -> RMSNorm:
     return RMSNorm(config.dim, config.norm_eps, config.use_kernels)
 
 
+def _halo(block: nn.Module, n: torch.Tensor, rows: int) -> tuple[torch.Tensor, int, int]:
+    """Under context parallelism: ``n`` with the previous shard's last ``rows``
+    rows prepended, their count, and the global index of the first row."""
+    cp = getattr(block, "cp", None)
+    if cp is None or not cp.active:
+        return n, 0, 0
+    ne, h = cp.extend(n, rows)
+    return ne, h, cp.start(n.shape[1]) - h
+
+
+def _conv_halo(config: TitansConfig) -> int:
+    return config.conv_kernel_size - 1 if config.use_conv else 0
+
+
 def _ffn_residual(block: nn.Module, x: torch.Tensor, h: torch.Tensor) -> torch.Tensor:
     """``x + dropout(ffn(h))``; the add runs in the FFN's last GEMM when dropout is off."""
     if block.dropout.p == 0.0 or not block.training:
@@ -69,6 +83,8 @@ class MACBlock(nn.Module):
 
 
 class MAGBlock(nn.Module):
+    cp = None  # ContextShard under context parallelism (parallel.context)
+
     def __init__(self, config: TitansConfig) -> None:
         super().__init__()
         self.config = config
@@ -86,13 +102,18 @@ class MAGBlock(nn.Module):
 
     def forward(self, x: torch.Tensor, state: MemoryState | None = None, update_memory: bool = True):
         n = self.norm1(x)
-        y = x + self.dropout(self.attention(n, prefix=self.persistent(x.shape[0])))
-        m, new_state = self.memory(n, state=state, update=update_memory)
+        # one halo serves the window (w - 1 rows) and the memory convolutions (K - 1)
+        ne, h, pos = _halo(self, n, max(self.config.window_size - 1, _conv_halo(self.config)))
+        y = x + self.dropout(self.attention(ne, prefix=self.persistent(x.shape[0]), context_rows=h,
+                                            position_offset=pos))
+        m, new_state = self.memory(ne, state=state, update=update_memory, context_rows=h)
         out = y * m
         return _ffn_residual(self, out, self.norm2(out)), new_state
 
 
 class MALBlock(nn.Module):
+    cp = None
+
     def __init__(self, config: TitansConfig) -> None:
         super().__init__()
         self.config = config
@@ -109,13 +130,18 @@ class MALBlock(nn.Module):
         return self.norm1(x)
 
     def forward(self, x: torch.Tensor, state: MemoryState | None = None, update_memory: bool = True):
-        m, new_state = self.memory(self.norm1(x), state=state, update=update_memory)
+        n1, h1, _ = _halo(self, self.norm1(x), _conv_halo(self.config))
+        m, new_state = self.memory(n1, state=state, update=update_memory, context_rows=h1)
         x, n2 = self.norm2.forward_with_residual(x, self.dropout(m))  # residual add fused with the norm
-        x, n3 = self.norm3.forward_with_residual(x, self.dropout(self.attention(n2, prefix=self.persistent(x.shape[0]))))
+        n2, h2, pos = _halo(self, n2, self.config.window_size - 1)
+        a = self.attention(n2, prefix=self.persistent(x.shape[0]), context_rows=h2, position_offset=pos)
+        x, n3 = self.norm3.forward_with_residual(x, self.dropout(a))
         return _ffn_residual(self, x, n3), new_state
 
 
 class LMMBlock(nn.Module):
+    cp = None
+
     def __init__(self, config: TitansConfig) -> None:
         super().__init__()
         self.config = config
@@ -129,7 +155,8 @@ class LMMBlock(nn.Module):
         return self.norm1(x)
 
     def forward(self, x: torch.Tensor, state: MemoryState | None = None, update_memory: bool = True):
-        m, new_state = self.memory(self.norm1(x), state=state, update=update_memory)
+        n1, h1, _ = _halo(self, self.norm1(x), _conv_halo(self.config))
+        m, new_state = self.memory(n1, state=state, update=update_memory, context_rows=h1)
         x, n2 = self.norm2.forward_with_residual(x, self.dropout(m))  # residual add fused with the norm
         return _ffn_residual(self, x, n2), new_state
 

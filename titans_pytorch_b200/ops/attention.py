@@ -13,6 +13,11 @@ One op serves both attention forms of the reference:
   rule with an infinite window, so the discarded prefix query rows are never
   computed.
 
+``pos_offset`` shifts the RoPE positions of the main rows (queries and main
+keys) to ``P + pos_offset + i`` while prefix keys keep ``0..P-1``: a sequence
+shard that starts at global token ``pos_offset`` then attends exactly as the
+same rows of the whole sequence would.
+
 RoPE is the interleaved-pair rotation of the reference (`attention.py:107-132`),
 base 10000, applied on load inside the CUDA kernel (``csrc/attention.cu``).
 """
@@ -64,7 +69,8 @@ def _split_qkv(qkv, pkv, H):
     return q, k, v, pk, pv
 
 
-def window_attention_reference(qkv, pkv, H, window, scale, inv_freq, dropout_p=0.0, training=False):
+def window_attention_reference(qkv, pkv, H, window, scale, inv_freq, dropout_p=0.0, training=False,
+                               pos_offset=0):
     """PyTorch restatement (dense mask + SDPA).  Returns [B, T, H, d]."""
     q, k, v, pk, pv = _split_qkv(qkv, pkv, H)
     B, T, _, d = q.shape
@@ -75,8 +81,9 @@ def window_attention_reference(qkv, pkv, H, window, scale, inv_freq, dropout_p=0
     else:
         kf, vf = k, v
     if inv_freq is not None:
-        cq, sq = rope_angles(torch.arange(P, P + T, device=q.device), inv_freq)
-        ck, sk = rope_angles(torch.arange(0, P + T, device=q.device), inv_freq)
+        main = torch.arange(P, P + T, device=q.device) + pos_offset
+        cq, sq = rope_angles(main, inv_freq)
+        ck, sk = rope_angles(torch.cat([torch.arange(0, P, device=q.device), main]), inv_freq)
         q = apply_rope_reference(q, cq, sq)
         kf = apply_rope_reference(kf, ck, sk)
     mask = prefix_window_mask(T, P, window, q.device)
@@ -91,15 +98,15 @@ class _WindowAttnFn(torch.autograd.Function):
     """pack (RoPE + head-major layout) -> flash forward; backward -> unpack."""
 
     @staticmethod
-    def forward(ctx, qkv, pkv, H, window, scale, inv_freq):
+    def forward(ctx, qkv, pkv, H, window, scale, inv_freq, pos_offset):
         E = ext()
-        Q, K, V = E.attn_pack(qkv, pkv, H, inv_freq)
+        Q, K, V = E.attn_pack(qkv, pkv, H, inv_freq, pos_offset)
         if E.attn_tc_fwd_supported(Q.shape[-1]):
             O, lse = E.attn_fwd_tc(Q, K, V, window, scale)      # tcgen05 / TMEM / TMA (head_dim 64, 96)
         else:
             O, lse = E.attn_fwd_packed(Q, K, V, window, scale)  # mma.sync path (other head dims)
         ctx.save_for_backward(Q, K, V, O, lse, inv_freq)
-        ctx.window, ctx.scale = window, scale
+        ctx.window, ctx.scale, ctx.pos_offset = window, scale, pos_offset
         ctx.bp = 0 if pkv is None else pkv.shape[0]
         ctx.dtype = qkv.dtype
         return O
@@ -112,19 +119,21 @@ class _WindowAttnFn(torch.autograd.Function):
             dQa, dKa, dVa = E.attn_bwd_tc(dO, Q, K, V, O, lse, ctx.window, ctx.scale)      # tcgen05
         else:
             dQa, dKa, dVa = E.attn_bwd_packed(dO, Q, K, V, O, lse, ctx.window, ctx.scale)  # mma.sync
-        dqkv, dpkv = E.attn_unpack(dQa, dKa, dVa, inv_freq, max(ctx.bp, 1), ctx.dtype)
-        return dqkv, (dpkv if ctx.bp else None), None, None, None, None
+        dqkv, dpkv = E.attn_unpack(dQa, dKa, dVa, inv_freq, max(ctx.bp, 1), ctx.dtype, ctx.pos_offset)
+        return dqkv, (dpkv if ctx.bp else None), None, None, None, None, None
 
 
 def window_attention(qkv: torch.Tensor, pkv: torch.Tensor | None, num_heads: int,
                      window: int | None = None, scale: float | None = None,
                      inv_freq: torch.Tensor | None = None, dropout_p: float = 0.0,
-                     training: bool = False, use_kernels: bool | None = None) -> torch.Tensor:
+                     training: bool = False, use_kernels: bool | None = None,
+                     pos_offset: int = 0) -> torch.Tensor:
     """Attention of the queries in ``qkv`` over ``[prefix || main]`` keys.
 
     ``qkv`` is the fused projection ``[B, T, 3D]`` (q | k | v, last dim
     contiguous); ``pkv`` the projected prefix ``[B or 1, P, 2D]`` (k | v) or
-    ``None``.  ``window=None`` means no window (MAC).  Returns ``[B, T, H, d]``.
+    ``None``.  ``window=None`` means no window (MAC).  ``pos_offset`` is the
+    global index of the first main row (RoPE only).  Returns ``[B, T, H, d]``.
     """
     window = NO_WINDOW if window is None else int(window)
     H = int(num_heads)
@@ -136,8 +145,9 @@ def window_attention(qkv: torch.Tensor, pkv: torch.Tensor | None, num_heads: int
         if dropout_p > 0.0 and training:
             raise NotImplementedError("attention-probability dropout is not implemented in the "
                                       "sm_100a attention kernel; set dropout=0")
-        return _WindowAttnFn.apply(qkv, pkv, H, window, scale, inv_freq)
-    return window_attention_reference(qkv, pkv, H, window, scale, inv_freq, dropout_p, training)
+        return _WindowAttnFn.apply(qkv, pkv, H, window, scale, inv_freq, int(pos_offset))
+    return window_attention_reference(qkv, pkv, H, window, scale, inv_freq, dropout_p, training,
+                                      int(pos_offset))
 
 
 def attention_flops(B: int, T: int, H: int, d: int, P: int, window: int | None) -> float:

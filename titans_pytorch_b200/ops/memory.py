@@ -286,53 +286,97 @@ def _memory_step_fused(k2, v2, weights, momentum, gates, act, linear_silu, B, T)
     return new_w, new_m
 
 
-def _memory_step_cuda(k, v, x_for_gates, weights, momentum, gate_ws, gate_bs, lr, mom, act,
-                      linear_silu):
-    """Device-resident update: gates kernel, then the fused tcgen05 path (bf16)
-    or PyTorch GEMMs with the extension's epilogue kernels."""
+def _memory_grads_cuda(k2, v2, weights, act, linear_silu, B, T):
+    """fp32 associative-loss gradients with PyTorch GEMMs and the extension's epilogue kernels."""
     E = ext()
-    gates = E.memory_gates(x_for_gates, list(gate_ws), list(gate_bs), float(lr), float(mom))
-    B, T, D = k.shape
-    k2 = k.reshape(-1, D)
-    v2 = v.reshape(-1, v.shape[-1])
-    if not k2.is_contiguous():
-        k2 = k2.contiguous()
-    if not v2.is_contiguous():
-        v2 = v2.contiguous()
-    if _fused_update_ok(k2, v2, weights, momentum, act) and want_kernels(k2):
-        return _memory_step_fused(k2, v2, list(weights), list(momentum), gates, act, linear_silu, B, T)
     L = len(weights)
     if L == 1 and linear_silu:
         h = torch.empty_like(k2)
         E.act_inplace(k2, h, act)
         pred = torch.mm(h, weights[0].t())
         E.scaled_err(pred, v2, 2.0 / (B * T))
-        grads = [torch.mm(pred.t(), h, out_dtype=torch.float32)]
-    else:
-        hs, zs = [k2], []
-        h = k2
-        for i, w in enumerate(weights):
-            z = torch.mm(h, w.t())
-            if i < L - 1:
-                a = torch.empty_like(z)
-                E.act_inplace(z, a, act)
-                zs.append(z)
-                hs.append(a)
-                h = a
-            else:
-                h = z
-        E.scaled_err(h, v2, 2.0 / h.numel())
-        delta = h
-        grads = [None] * L
-        for i in range(L - 1, -1, -1):
-            grads[i] = torch.mm(delta.t(), hs[i], out_dtype=torch.float32)
-            if i > 0:
-                nd = torch.mm(delta, weights[i])
-                E.act_grad_mul(nd, zs[i - 1], act)
-                delta = nd
+        return [torch.mm(pred.t(), h, out_dtype=torch.float32)]
+    hs, zs = [k2], []
+    h = k2
+    for i, w in enumerate(weights):
+        z = torch.mm(h, w.t())
+        if i < L - 1:
+            a = torch.empty_like(z)
+            E.act_inplace(z, a, act)
+            zs.append(z)
+            hs.append(a)
+            h = a
+        else:
+            h = z
+    E.scaled_err(h, v2, 2.0 / h.numel())
+    delta = h
+    grads = [None] * L
+    for i in range(L - 1, -1, -1):
+        grads[i] = torch.mm(delta.t(), hs[i], out_dtype=torch.float32)
+        if i > 0:
+            nd = torch.mm(delta, weights[i])
+            E.act_grad_mul(nd, zs[i - 1], act)
+            delta = nd
+    return grads
+
+
+def _flat_kv(k, v):
+    D = k.shape[-1]
+    k2 = k.reshape(-1, D)
+    v2 = v.reshape(-1, v.shape[-1])
+    return (k2 if k2.is_contiguous() else k2.contiguous()), (v2 if v2.is_contiguous() else v2.contiguous())
+
+
+def _apply_update(weights, momentum, grads, gates):
+    E = ext()
     new_w, new_m = [], []
     for w, m, g in zip(weights, momentum, grads, strict=True):
         w2, m2 = E.mem_update(w, m, g, gates)
         new_w.append(w2)
         new_m.append(m2)
     return new_w, new_m
+
+
+def _memory_step_cuda(k, v, x_for_gates, weights, momentum, gate_ws, gate_bs, lr, mom, act,
+                      linear_silu):
+    """Device-resident update: gates kernel, then the fused tcgen05 path (bf16)
+    or PyTorch GEMMs with the extension's epilogue kernels."""
+    E = ext()
+    gates = E.memory_gates(x_for_gates, list(gate_ws), list(gate_bs), float(lr), float(mom))
+    B, T, _ = k.shape
+    k2, v2 = _flat_kv(k, v)
+    if _fused_update_ok(k2, v2, weights, momentum, act) and want_kernels(k2):
+        return _memory_step_fused(k2, v2, list(weights), list(momentum), gates, act, linear_silu, B, T)
+    return _apply_update(weights, momentum, _memory_grads_cuda(k2, v2, weights, act, linear_silu, B, T), gates)
+
+
+@torch.no_grad()
+def memory_step_sharded(k, v, x_for_gates, weights, momentum, gate_ws, gate_bs, lr: float, mom: float,
+                        act: str, linear_silu: bool, use_kernels, shard):
+    """:func:`memory_step` of a sequence split over the ranks of ``shard``
+    (a :class:`titans_pytorch_b200.parallel.context.ContextShard`).
+
+    Each rank holds ``T`` of the sequence's tokens.  The gates read the mean of
+    the memory input over the whole sequence and the gradient is the mean of
+    per-token terms over the whole sequence; with equal shards both are the
+    average over ranks of the shard's own value, so two all-reduces give every
+    rank the state the unsharded update computes.
+    """
+    x_mean = x_for_gates.float().mean(dim=1, keepdim=True)
+    shard.all_reduce_mean_(x_mean)
+    x_mean = x_mean.to(x_for_gates.dtype)
+    B, T, _ = k.shape
+    cuda = want_kernels(k, use_kernels)
+    if cuda:
+        grads = _memory_grads_cuda(*_flat_kv(k, v), weights, act, linear_silu, B, T)
+    else:
+        grads = [g.float() for g in memory_grads_reference(k, v, weights, act, linear_silu)]
+    flat = torch.cat([g.reshape(-1) for g in grads])
+    shard.all_reduce_mean_(flat)
+    grads = [t.view_as(g) for t, g in zip(flat.split([g.numel() for g in grads]), grads, strict=True)]
+    if cuda:
+        gates = ext().memory_gates(x_mean, list(gate_ws), list(gate_bs), float(lr), float(mom))
+        return _apply_update(weights, momentum, grads, gates)
+    alpha, theta, eta = memory_gates_reference(x_mean, gate_ws, gate_bs, lr, mom)
+    grads = [g.to(w.dtype) for g, w in zip(grads, weights, strict=True)]
+    return memory_update_reference(weights, momentum, grads, alpha, eta, theta)

@@ -131,7 +131,12 @@ def enable_gradient_checkpointing(model: torch.nn.Module) -> torch.nn.Module:
                 if state is None:
                     state = mem.init_state(x.shape[0], x.device)
                 with torch.no_grad():
-                    new_state = mem._update(_blk.memory_input(x), state)
+                    n = _blk.memory_input(x)
+                    h = 0
+                    if getattr(_blk, "cp", None) is not None:  # context parallel: the convolutions' halo
+                        from ..models.titans import _conv_halo, _halo
+                        n, h, _ = _halo(_blk, n, _conv_halo(_blk.config))
+                    new_state = mem._update(n, state, h)
                 out = checkpoint(lambda xx, st: _fwd(xx, st, update_memory=False)[0], x, state, use_reentrant=False)
                 return out, new_state
         else:

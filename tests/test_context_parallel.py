@@ -150,6 +150,31 @@ def test_gpu_attention_position_offset(hd):
     assert (o0.float() - o.detach().float()).abs().max() > 1e-2
 
 
+@pytest.mark.gpu
+@pytest.mark.parametrize("layers", [1, 2, 3])
+def test_gpu_sharded_memory_step_one_rank(layers):
+    """On one shard the sharded update (tcgen05 gradients in fp32, then the
+    update kernel) equals the fused update."""
+    from titans_pytorch_b200.ops.memory import memory_step, memory_step_sharded
+
+    torch.manual_seed(0)
+    B, T_, D, Hd = 2, 1024, 256, 512
+    dev, bf = "cuda", torch.bfloat16
+    k = torch.nn.functional.normalize(torch.randn(B, T_, D, device=dev), dim=-1).to(bf)
+    v = torch.randn(B, T_, D, device=dev, dtype=bf)
+    x = torch.randn(B, T_, D, device=dev, dtype=bf)
+    dims = [D, D] if layers == 1 else [D] + [Hd] * (layers - 1) + [D]
+    ws = [(torch.randn(dims[i + 1], dims[i], device=dev) * 0.05).to(bf) for i in range(layers)]
+    ms = [(torch.randn_like(w.float()) * 0.01).to(bf) for w in ws]
+    gw = [(torch.randn(D, D, device=dev) * 0.02).to(bf) for _ in range(3)]
+    gb = [torch.zeros(D, device=dev, dtype=bf) for _ in range(3)]
+    lin = layers == 1
+    w1, m1 = memory_step(k, v, x, ws, ms, gw, gb, 0.1, 0.9, "silu", lin)
+    w2, m2 = memory_step_sharded(k, v, x, ws, ms, gw, gb, 0.1, 0.9, "silu", lin, None, ContextShard())
+    for a, b in zip(w1 + m1, w2 + m2, strict=True):
+        torch.testing.assert_close(b.float(), a.float(), atol=2e-3, rtol=2e-2)
+
+
 def _gpu_cp_worker(rank, world, out_dir, cls, S):
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),

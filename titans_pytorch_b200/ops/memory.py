@@ -320,6 +320,30 @@ def _memory_grads_cuda(k2, v2, weights, act, linear_silu, B, T):
     return grads
 
 
+def _memory_grads_tc(k2, v2, weights, act, linear_silu, B, T):
+    """fp32 associative-loss gradients on the tcgen05 GEMM: the fused update's
+    forward (act epilogues), error and act' back-propagation, with the weight
+    gradients stored in fp32 instead of applied (the caller reduces them first)."""
+    L = len(weights)
+    if L == 1 and linear_silu:
+        h = torch.empty_like(k2)
+        ext().act_inplace(k2, h, act)
+        return [G.mm_wgrad(G.mm_err(h, weights[0], v2, 2.0 / (B * T)), h, fp32=True)]
+    hs, zs = [k2], []
+    h = k2
+    for w in weights[:-1]:
+        z, h = G.mm_act(h, w, act)
+        zs.append(z)
+        hs.append(h)
+    delta = G.mm_err(h, weights[-1], v2, 2.0 / (k2.shape[0] * weights[-1].shape[0]))
+    grads = [None] * L
+    for i in range(L - 1, -1, -1):
+        grads[i] = G.mm_wgrad(delta, hs[i], fp32=True)
+        if i > 0:
+            delta = G.mm_act_grad(delta, weights[i], zs[i - 1], act)
+    return grads
+
+
 def _flat_kv(k, v):
     D = k.shape[-1]
     k2 = k.reshape(-1, D)
@@ -368,7 +392,9 @@ def memory_step_sharded(k, v, x_for_gates, weights, momentum, gate_ws, gate_bs, 
     B, T, _ = k.shape
     cuda = want_kernels(k, use_kernels)
     if cuda:
-        grads = _memory_grads_cuda(*_flat_kv(k, v), weights, act, linear_silu, B, T)
+        k2, v2 = _flat_kv(k, v)
+        tc = _fused_update_ok(k2, v2, weights, momentum, act)
+        grads = (_memory_grads_tc if tc else _memory_grads_cuda)(k2, v2, weights, act, linear_silu, B, T)
     else:
         grads = [g.float() for g in memory_grads_reference(k, v, weights, act, linear_silu)]
     flat = torch.cat([g.reshape(-1) for g in grads])

@@ -383,12 +383,10 @@ def memory_step_sharded(k, v, x_for_gates, weights, momentum, gate_ws, gate_bs, 
     Each rank holds ``T`` of the sequence's tokens.  The gates read the mean of
     the memory input over the whole sequence and the gradient is the mean of
     per-token terms over the whole sequence; with equal shards both are the
-    average over ranks of the shard's own value, so two all-reduces give every
-    rank the state the unsharded update computes.
+    average over ranks of the shard's own value, so one all-reduce of both (in
+    one fp32 buffer) gives every rank the state the unsharded update computes.
     """
     x_mean = x_for_gates.float().mean(dim=1, keepdim=True)
-    shard.all_reduce_mean_(x_mean)
-    x_mean = x_mean.to(x_for_gates.dtype)
     B, T, _ = k.shape
     cuda = want_kernels(k, use_kernels)
     if cuda:
@@ -397,9 +395,11 @@ def memory_step_sharded(k, v, x_for_gates, weights, momentum, gate_ws, gate_bs, 
         grads = (_memory_grads_tc if tc else _memory_grads_cuda)(k2, v2, weights, act, linear_silu, B, T)
     else:
         grads = [g.float() for g in memory_grads_reference(k, v, weights, act, linear_silu)]
-    flat = torch.cat([g.reshape(-1) for g in grads])
+    parts = [x_mean] + grads
+    flat = torch.cat([t.reshape(-1) for t in parts])
     shard.all_reduce_mean_(flat)
-    grads = [t.view_as(g) for t, g in zip(flat.split([g.numel() for g in grads]), grads, strict=True)]
+    x_mean, *grads = [t.view_as(g) for t, g in zip(flat.split([t.numel() for t in parts]), parts, strict=True)]
+    x_mean = x_mean.to(x_for_gates.dtype)
     if cuda:
         gates = ext().memory_gates(x_mean, list(gate_ws), list(gate_bs), float(lr), float(mom))
         return _apply_update(weights, momentum, grads, gates)

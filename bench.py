@@ -206,7 +206,7 @@ def count_launches(step_fn, prefixes) -> tuple[int, int]:
 
 
 # ---------------------------------------------------------------------------- arms
-def build_ours(device, world, parallel="dp", overlap=True, reshard=True):
+def build_ours(device, world, parallel="dp", overlap=True, reshard=True, wavefront=0):
     from titans_pytorch_b200 import TitansConfig, create_model
     from titans_pytorch_b200.train.trainer import Trainer, TrainStepConfig
     from titans_pytorch_b200.utils.perf import enable_gradient_checkpointing
@@ -215,6 +215,10 @@ def build_ours(device, world, parallel="dp", overlap=True, reshard=True):
     model = create_model(CFG["model"], TitansConfig(**MODEL_FIELDS))
     if CFG["ckpt"]:
         enable_gradient_checkpointing(model)
+    if wavefront > 1 and CFG["model"] == "mac":
+        from titans_pytorch_b200.utils.perf import enable_wavefront
+
+        enable_wavefront(model, wavefront)
     engine = None
     if world > 1 and parallel == "fsdp":
         from titans_pytorch_b200.parallel.fsdp import FullyShardedEngine
@@ -325,6 +329,9 @@ def main():
                     help="fsdp: full = FULL_SHARD (parameters gathered per use into working slots, gradients "
                          "reduce-scattered per block during the backward); grad-op = SHARD_GRAD_OP (gathered "
                          "parameters kept until the step)")
+    ap.add_argument("--wavefront", type=int, default=0,
+                    help="mac400m: run the (layer, segment) loop as a wavefront on this many CUDA streams "
+                         "(0 = sequential)")
     args = ap.parse_args()
     global CFG, MODEL_FIELDS, SEQ, MICRO_BATCH
     CFG = CONFIGS[args.config]
@@ -349,7 +356,7 @@ def main():
     else:
         overlap = args.overlap == "on" or (args.overlap == "auto" and args.parallel == "fsdp")
         trainer, nparams = build_ours(device, world, args.parallel, overlap=overlap,
-                                      reshard=args.fsdp_mode == "full")
+                                      reshard=args.fsdp_mode == "full", wavefront=args.wavefront)
         prefixes = ("tb::",)
 
     batches = make_batches(world, rank, W + K + 1)
@@ -414,6 +421,8 @@ def main():
                              f"reduce-scatter {when}; fused AdamW shard)")
                        if args.parallel == "fsdp"
                        else f"dp{world} (peer-memory reduce-scatter {when}; fused AdamW shard / all-gather)")
+    if args.impl == "ours" and args.wavefront > 1 and CFG["model"] == "mac":
+        parallelism += f"; (layer, segment) wavefront on {args.wavefront} streams"
     peak = torch.cuda.max_memory_allocated(device)
     comm = getattr(getattr(trainer, "optimizer", None), "comm_bytes", None)
     peak_gib = (peak + (comm() if comm is not None else 0)) / 2 ** 30

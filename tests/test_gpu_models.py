@@ -220,3 +220,36 @@ def test_side_stream_weight_grads_match_main_stream(kind):
         runs.append({k: v.float().clone() for k, v in tr.model.state_dict().items()})
     for k in runs[0]:
         torch.testing.assert_close(runs[0][k], runs[1][k], atol=5e-3, rtol=1e-2, msg=k)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("graph", [False, True])
+def test_mac_wavefront_matches_sequential(graph):
+    """The (layer, segment) wavefront on two streams trains like the sequential loop."""
+    import copy
+
+    from titans_pytorch_b200.train.trainer import Trainer, TrainStepConfig
+    from titans_pytorch_b200.utils.perf import enable_wavefront
+
+    fields = dict(dim=256, num_heads=4, num_layers=4, vocab_size=512, chunk_size=64, window_size=64,
+                  num_persistent_tokens=4, dropout=0.0, max_seq_len=512, num_memory_layers=2, ffn_mult=2.0)
+    torch.manual_seed(0)
+    base = T.TitansMAC(T.TitansConfig(**fields))
+    seq, wav = copy.deepcopy(base), enable_wavefront(copy.deepcopy(base), 2)
+    dev = torch.device("cuda")
+    cfg = TrainStepConfig(lr=1e-3, cuda_graph=graph, graph_warmup=1)
+    trs, trw = Trainer(seq, cfg, device=dev), Trainer(wav, cfg, device=dev)
+    g = torch.Generator().manual_seed(3)
+    for _ in range(3):
+        d = torch.randint(0, 512, (2, 257), generator=g)
+        b = {"input_ids": d[:, :-1], "labels": d[:, 1:]}
+        ls, lw = trs.train_step(b), trw.train_step(b)
+        torch.testing.assert_close(lw.float(), ls.float(), atol=2e-3, rtol=2e-3)
+    torch.cuda.synchronize()
+    with torch.no_grad():
+        for (n, a), (_, w) in zip(seq.named_parameters(), wav.named_parameters(), strict=True):
+            torch.testing.assert_close(w.float(), a.float(), atol=2e-3, rtol=2e-2, msg=n)
+        ids = torch.randint(0, 512, (2, 256), generator=g).to(dev)
+        ref, _ = seq(ids)
+        out, _ = wav(ids)
+    torch.testing.assert_close(out.float(), ref.float(), atol=3e-2, rtol=3e-2)

@@ -210,6 +210,9 @@ class TitansMAC(_TitansLM):
     block_cls = MACBlock
     model_type = "mac"
 
+    # Streams of the (layer, segment) wavefront; 0 = the sequential loop.
+    wavefront_streams = 0
+
     def hidden_states(self, input_ids: torch.Tensor, states=None):
         if states is None:
             states = [None] * len(self.blocks)
@@ -219,12 +222,74 @@ class TitansMAC(_TitansLM):
         self._wcache.clear()
         self._wcache["active"] = True  # only while this forward runs
         try:
-            for s in range(0, x.shape[1], cs):
-                chunk, states = self._run_blocks(x[:, s:s + cs], states)
-                outs.append(chunk)
+            if self.wavefront_streams > 1 and x.is_cuda and x.shape[1] > cs and len(self.blocks) > 1:
+                outs, states = self._wavefront(x, list(states))
+            else:
+                for s in range(0, x.shape[1], cs):
+                    chunk, states = self._run_blocks(x[:, s:s + cs], states)
+                    outs.append(chunk)
         finally:
             self._wcache.clear()  # weights change between forwards
         return self.norm(torch.cat(outs, dim=1)), states
+
+    def _wavefront(self, x: torch.Tensor, states: list):
+        """The chunk loop as a (layer, segment) wavefront on CUDA streams.
+
+        Block i on segment c needs block i-1's output on segment c and block
+        i's memory state after segment c-1, nothing else (the reference's loop,
+        `src/titans/models.py:301-314`, runs the same pairs one at a time).
+        Block i runs on stream ``i mod n`` in segment order, and an event
+        orders it after block i-1 on the same segment, so the pairs of one
+        anti-diagonal (i + c constant) can run at the same time.  Every block
+        still sees its segments in order, which also keeps the in-place writes
+        of the memory state into its parameters in the sequential order.  The
+        backward runs each op on its forward op's stream; :meth:`join_streams`
+        makes the current stream wait for all of them.
+        """
+        main = torch.cuda.current_stream(x.device)
+        streams = self._streams(x.device)
+        for st in streams:
+            st.wait_stream(main)
+        cs = self.config.chunk_size
+        cur = [x[:, s:s + cs] for s in range(0, x.shape[1], cs)]
+        ready = [None] * len(cur)
+        L = len(self.blocks)
+        for d in range(len(cur) + L - 1):
+            for i in range(max(0, d - len(cur) + 1), min(d, L - 1) + 1):
+                c = d - i
+                st = streams[i % len(streams)]
+                with torch.cuda.stream(st):
+                    if ready[c] is not None:
+                        st.wait_event(ready[c])
+                    cur[c].record_stream(st)  # made on another stream: keep it until this one is done
+                    out, states[i] = self.blocks[i](cur[c], state=states[i])
+                    ev = torch.cuda.Event()
+                    ev.record(st)
+                cur[c], ready[c] = out, ev
+        self.join_streams()
+        for t in cur:
+            t.record_stream(main)
+        for st_ in states:
+            for t in st_.weights + st_.momentum:
+                t.record_stream(main)
+        return cur, states
+
+    def _streams(self, device) -> list:
+        n = int(self.wavefront_streams)
+        have = getattr(self, "_wf_streams", None)
+        if not have or len(have) != n or have[0].device != device:
+            self._wf_streams = [torch.cuda.Stream(device) for _ in range(n)]
+        return self._wf_streams
+
+    def join_streams(self) -> None:
+        """Make the current stream wait for the wavefront streams (after a
+        forward, and after the backward before anything reads gradients)."""
+        streams = getattr(self, "_wf_streams", None)
+        if not streams:
+            return
+        main = torch.cuda.current_stream(streams[0].device)
+        for st in streams:
+            main.wait_stream(st)
 
 
 class TitansMAG(_TitansLM):

@@ -81,6 +81,10 @@ class Trainer:
         # small weight gradients on a second stream, unless the engine reads the
         # gradients during the backward (reductions of finished blocks)
         self._side_wgrad = self.device.type == "cuda" and not getattr(self.optimizer, "reduces_during_backward", False)
+        if getattr(self.model, "wavefront_streams", 0) > 1 and getattr(self.optimizer, "reduces_during_backward",
+                                                                        False):
+            raise ValueError("the MAC wavefront runs the backward on several streams; use an engine that "
+                             "reduces the gradients after the backward")
         self._graph = None
         self._eager_graph_steps = 0
         if self.cfg.cuda_graph:
@@ -113,12 +117,18 @@ class Trainer:
         prep = getattr(self.optimizer, "prepare_backward", None)
         if prep is not None:  # engines that reduce during the backward: is this the step's last one?
             prep((self._micro + 1) % accum == 0)
-        with accumulate_weight_grads(side_stream=self._side_wgrad):
-            (loss / accum if accum > 1 else loss).backward()
+        self._backward(loss / accum if accum > 1 else loss)
         self._micro += 1
         if self._micro % accum == 0:
             self.optimizer_step()
         return loss.detach()
+
+    def _backward(self, loss: torch.Tensor) -> None:
+        with accumulate_weight_grads(side_stream=self._side_wgrad):
+            loss.backward()
+            join = getattr(self.model, "join_streams", None)
+            if join is not None:  # a model whose forward (so its backward) used several streams
+                join()
 
     # ------------------------------------------------------------ CUDA graph
     def _schedule(self):
@@ -141,8 +151,7 @@ class Trainer:
                 ids = self._to_device(batch["input_ids"])
                 labels = self._to_device(batch["labels"])
                 loss = self.loss_fn(ids, labels)
-                with accumulate_weight_grads(side_stream=self._side_wgrad):
-                    loss.backward()
+                self._backward(loss)
                 self.optimizer_step()
             cur.wait_stream(side)
             self._eager_graph_steps += 1
@@ -168,8 +177,7 @@ class Trainer:
         saved_count = opt.step_count
         with torch.cuda.graph(g):
             loss = self.loss_fn(self._static_ids, self._static_labels)
-            with accumulate_weight_grads(side_stream=self._side_wgrad):
-                loss.backward()
+            self._backward(loss)
             if self.engine is not None:
                 self.engine.reduce_gradients(opt)
             opt.step(hyper=self._hyper, schedule=sched)

@@ -107,6 +107,17 @@ def empty_cache_if_needed(threshold: float = 0.9) -> None:
             torch.cuda.empty_cache()
 
 
+def enable_wavefront(model: torch.nn.Module, streams: int = 2) -> torch.nn.Module:
+    """Run a MAC model's (layer, segment) loop as a wavefront on ``streams``
+    CUDA streams (``streams <= 1``: the sequential loop).  The result is the
+    sequential loop's; the pairs (i, c) with equal i + c may run concurrently,
+    which fills the GPU better when each segment's kernels are small."""
+    if getattr(model, "model_type", None) != "mac":
+        raise ValueError("the wavefront schedule is for MAC models (segments x layers)")
+    model.wavefront_streams = int(streams)
+    return model
+
+
 def enable_gradient_checkpointing(model: torch.nn.Module) -> torch.nn.Module:
     """Recompute each block's forward in the backward (non-reentrant checkpoint).
 

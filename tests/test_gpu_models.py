@@ -246,9 +246,20 @@ def test_mac_wavefront_matches_sequential(graph):
         ls, lw = trs.train_step(b), trw.train_step(b)
         torch.testing.assert_close(lw.float(), ls.float(), atol=2e-3, rtol=2e-3)
     torch.cuda.synchronize()
+    # The gradients (through AdamW's first moments, one segment per parameter) agree to
+    # rounding; the parameters only to AdamW's step size, because a gradient near zero
+    # can change sign under a different fp32 accumulation order.
+    ms, mw = trs.optimizer.exp_avg, trw.optimizer.exp_avg
+    worst = (0.0, "")
+    space = trs.optimizer.space
+    for i, (p, o) in enumerate(zip(space.params, space.offsets, strict=True)):
+        a, w = ms[o:o + p.numel()], mw[o:o + p.numel()]
+        err = ((w - a).norm() / a.norm().clamp_min(1e-20)).item()
+        worst = max(worst, (err, f"param {i} {tuple(p.shape)}"))
+    assert worst[0] < 2e-2, worst
     with torch.no_grad():
         for (n, a), (_, w) in zip(seq.named_parameters(), wav.named_parameters(), strict=True):
-            torch.testing.assert_close(w.float(), a.float(), atol=2e-3, rtol=2e-2, msg=n)
+            torch.testing.assert_close(w.float(), a.float(), atol=3 * 2 * cfg.lr, rtol=0, msg=n)
         ids = torch.randint(0, 512, (2, 256), generator=g).to(dev)
         ref, _ = seq(ids)
         out, _ = wav(ids)

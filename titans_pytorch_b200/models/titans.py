@@ -206,6 +206,26 @@ class _TitansLM(nn.Module):
         return linear(h, self.head.weight, use_kernels=self.config.use_kernels), new_states
 
 
+class _StreamHandoff(torch.autograd.Function):
+    """Identity at a stream boundary of the wavefront: ``x`` made on stream
+    ``src`` is read on ``dst`` (the stream current in the forward).  Both
+    directions tell the caching allocator about the other stream, so neither
+    the activation nor its gradient (made on ``dst`` in the backward, read by
+    the producer's backward on ``src``) is reused while the reader may still
+    run."""
+
+    @staticmethod
+    def forward(ctx, x, src, dst):
+        x.record_stream(dst)
+        ctx.src = src
+        return x.view_as(x)
+
+    @staticmethod
+    def backward(ctx, g):
+        g.record_stream(ctx.src)
+        return g, None, None
+
+
 class TitansMAC(_TitansLM):
     block_cls = MACBlock
     model_type = "mac"
@@ -253,6 +273,7 @@ class TitansMAC(_TitansLM):
         cs = self.config.chunk_size
         cur = [x[:, s:s + cs] for s in range(0, x.shape[1], cs)]
         ready = [None] * len(cur)
+        made_on = [main] * len(cur)
         L = len(self.blocks)
         for d in range(len(cur) + L - 1):
             for i in range(max(0, d - len(cur) + 1), min(d, L - 1) + 1):
@@ -261,14 +282,13 @@ class TitansMAC(_TitansLM):
                 with torch.cuda.stream(st):
                     if ready[c] is not None:
                         st.wait_event(ready[c])
-                    cur[c].record_stream(st)  # made on another stream: keep it until this one is done
-                    out, states[i] = self.blocks[i](cur[c], state=states[i])
+                    inp = cur[c] if made_on[c] is st else _StreamHandoff.apply(cur[c], made_on[c], st)
+                    out, states[i] = self.blocks[i](inp, state=states[i])
                     ev = torch.cuda.Event()
                     ev.record(st)
-                cur[c], ready[c] = out, ev
+                cur[c], ready[c], made_on[c] = out, ev, st
         self.join_streams()
-        for t in cur:
-            t.record_stream(main)
+        cur = [_StreamHandoff.apply(t, src, main) for t, src in zip(cur, made_on, strict=True)]
         for st_ in states:
             for t in st_.weights + st_.momentum:
                 t.record_stream(main)

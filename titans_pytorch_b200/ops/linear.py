@@ -176,6 +176,10 @@ def weight_grads(weights, dy2: torch.Tensor, x2: torch.Tensor, kern: bool, need)
     if target is not None:
         if kern and G.operand_ok(target) and _side_ok(dy2, target):
             side = _STATE["side"]
+            # The side stream reads its own copy of the output gradient: autograd may
+            # later sum another contribution into the incoming gradient tensor in place
+            # (when it holds the last reference), which must not race with this read.
+            dy2 = dy2.clone()
             side.wait_stream(torch.cuda.current_stream())
             with torch.cuda.stream(side):
                 G.mm_wgrad(dy2, x2, out=target, accumulate=True)

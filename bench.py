@@ -329,9 +329,10 @@ def main():
                     help="fsdp: full = FULL_SHARD (parameters gathered per use into working slots, gradients "
                          "reduce-scattered per block during the backward); grad-op = SHARD_GRAD_OP (gathered "
                          "parameters kept until the step)")
-    ap.add_argument("--wavefront", type=int, default=0,
+    ap.add_argument("--wavefront", type=int, default=-1,
                     help="mac400m: run the (layer, segment) loop as a wavefront on this many CUDA streams "
-                         "(0 = sequential)")
+                         "(0 = sequential; default: 2 where the gradients are reduced after the backward, "
+                         "i.e. one GPU or dp without overlap)")
     args = ap.parse_args()
     global CFG, MODEL_FIELDS, SEQ, MICRO_BATCH
     CFG = CONFIGS[args.config]
@@ -355,6 +356,8 @@ def main():
         prefixes = ()
     else:
         overlap = args.overlap == "on" or (args.overlap == "auto" and args.parallel == "fsdp")
+        if args.wavefront < 0:
+            args.wavefront = 2 if world == 1 or (args.parallel == "dp" and not overlap) else 0
         trainer, nparams = build_ours(device, world, args.parallel, overlap=overlap,
                                       reshard=args.fsdp_mode == "full", wavefront=args.wavefront)
         prefixes = ("tb::",)

@@ -107,6 +107,9 @@ def build_parser() -> argparse.ArgumentParser:
     a("--compile-mode", type=str, default="reduce-overhead",
       help="with --torch-compile: reduce-overhead / max-autotune / default all mean CUDA-graph replay")
     a("--gradient-checkpointing", action="store_true")
+    a("--wavefront", type=int, default=0,
+      help="MAC: run the (layer, segment) loop as a wavefront on this many CUDA streams (0 = sequential; "
+           "not with --parallel fsdp)")
     a("--heartbeat-timeout", type=float, default=60.0,
       help="under torchrun: seconds without a peer's heartbeat before this rank stops with an error")
     a("--dist-timeout", type=float, default=600.0, help="process-group timeout (seconds)")
@@ -199,6 +202,10 @@ def run(args) -> dict:
             raise SystemExit(f"--parallel cp: --seq-len {args.seq_len} must be divisible by {world} ranks")
     if args.gradient_checkpointing:
         enable_gradient_checkpointing(model)
+    if args.wavefront > 1 and args.model == "mac" and device.type == "cuda":
+        from ..utils.perf import enable_wavefront
+
+        enable_wavefront(model, args.wavefront)
     ds, eval_ds = split_eval(args, build_dataset(args, cfg.vocab_size), cfg.vocab_size)
     # context parallel: every rank reads the same whole sequences and keeps its shard of them
     dworld, drank = (1, 0) if cp is not None else (world, rank)

@@ -48,11 +48,15 @@ def _run(model, batch, reduce_grads=None):
     return logits.detach(), states, grads, logits2, states2
 
 
-def _cp_worker(rank, world, out_dir, cls, fields, S):
+def _cp_worker(rank, world, out_dir, cls, fields, S, ckpt=False):
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
     torch.manual_seed(0)
     model = getattr(T, cls)(T.TitansConfig(**fields, use_kernels=False))
     shard = enable_context_parallel(model)
+    if ckpt:  # the memory update then runs outside the recomputed region, with its own halo
+        from titans_pytorch_b200.utils.perf import enable_gradient_checkpointing
+
+        enable_gradient_checkpointing(model)
     assert (shard.rank, shard.world) == (rank, world)
     part = shard_batch(_batch(2, S, seed=3), shard)
 
@@ -74,10 +78,11 @@ def _cp_worker(rank, world, out_dir, cls, fields, S):
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("cls,world,S", [("TitansMAG", 2, 32), ("TitansMAL", 2, 32), ("TitansLMM", 2, 32),
-                                         ("TitansMAG", 4, 32)])
-def test_context_parallel_matches_whole_sequence(tmp_path, cls, world, S):
-    run_workers(_cp_worker, world, (str(tmp_path), cls, FIELDS, S))
+@pytest.mark.parametrize("cls,world,S,ckpt", [("TitansMAG", 2, 32, False), ("TitansMAL", 2, 32, False),
+                                              ("TitansLMM", 2, 32, False), ("TitansMAG", 4, 32, False),
+                                              ("TitansMAG", 2, 32, True), ("TitansMAL", 2, 32, True)])
+def test_context_parallel_matches_whole_sequence(tmp_path, cls, world, S, ckpt):
+    run_workers(_cp_worker, world, (str(tmp_path), cls, FIELDS, S, ckpt))
     torch.manual_seed(0)
     model = getattr(T, cls)(T.TitansConfig(**FIELDS, use_kernels=False))
     logits, states, grads, logits2, states2 = _run(model, _batch(2, S, seed=3))

@@ -6,7 +6,8 @@
   scheduler and RNG restored);
 * ``--eval-every`` evaluates a held-out set, logs ``val/loss`` and keeps
   ``best_model.pt``; fp16 is refused; ``--torch-compile`` on CPU runs eagerly;
-* ``--parallel cp`` trains with every sequence split over two gloo ranks.
+* ``--parallel cp`` trains with every sequence split over two gloo ranks;
+* ``--parallel pp`` trains MAC as a two-stage pipeline, with checkpoint and resume.
 """
 
 from __future__ import annotations
@@ -65,6 +66,29 @@ def test_context_parallel_cli(tmp_path):
     assert losses and all(0 < v < 20 for v in losses)
     assert any("val/loss" in x for x in lines)
     assert (ck / "final_model.pt").exists()
+
+
+def test_pipeline_cli_resume(tmp_path):
+    """--parallel pp (MAC over two gloo stages): the checkpoint gathers both stages'
+    weights into the model file, keeps one optimizer file per stage, and resuming
+    from it reproduces the uninterrupted run."""
+    a, b = tmp_path / "a", tmp_path / "b"
+    mac = [x if x != "mag" else "mac" for x in COMMON]
+    base = mac + ["--parallel", "pp", "--max-steps", "4", "--eval-every", "2", "--eval-batches", "1",
+                  "--heartbeat-timeout", "30", "--dist-timeout", "60"]
+    run_workers(_rank_main, 2, (base + ["--checkpoint-dir", str(a), "--save-every", "2"],), timeout=240)
+    mid = a / "step_2.pt"
+    for r in range(2):
+        assert (a / f"step_2.pt.optim.rank{r}-of-2").exists()
+    wm, wa = _weights(mid), _weights(a / "final_model.pt")
+    for blk in (0, 1):  # both stages trained between the two files, and rank 0's files hold both
+        k = f"blocks.{blk}.ffn.down_proj.weight"
+        assert not torch.allclose(wa[k].float(), wm[k].float()), k
+    run_workers(_rank_main, 2, (base + ["--checkpoint-dir", str(b), "--save-every", "0", "--resume", str(mid)],),
+                timeout=240)
+    wb = _weights(b / "final_model.pt")
+    for k in wa:
+        torch.testing.assert_close(wb[k], wa[k], rtol=1e-5, atol=1e-6, msg=k)
 
 
 def test_eval_loop_and_best_model(tmp_path):

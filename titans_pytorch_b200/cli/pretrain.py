@@ -84,10 +84,11 @@ def build_parser() -> argparse.ArgumentParser:
     a("--weight-decay", type=float, default=0.1)
     a("--grad-clip", type=float, default=1.0)
     a("--warmup-ratio", type=float, default=0.03)
-    a("--parallel", choices=["dp", "fsdp", "cp"], default="dp",
+    a("--parallel", choices=["dp", "fsdp", "cp", "pp"], default="dp",
       help="under torchrun: dp = replicated weights with the optimizer state sharded; fsdp = parameters "
            "sharded per block, all-gathered in the forward; cp = context parallel (MAG/MAL/LMM): every "
-           "sequence split over the ranks, halos exchanged, memory updates averaged")
+           "sequence split over the ranks, halos exchanged, memory updates averaged; pp = pipeline "
+           "(MAC): layers split into stages, one per rank, segments as micro-batches")
     a("--mixed-precision", choices=["none", "fp16", "bf16"], default="bf16",
       help="bf16 (default) or none (fp32); fp16 is rejected: the kernels compute in bf16")
     a("--checkpoint-dir", type=str, default="checkpoints")
@@ -163,7 +164,12 @@ def setup_distributed(args, device):
     os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
     dist.init_process_group("nccl" if device.type == "cuda" else "gloo",
                             timeout=datetime.timedelta(seconds=args.dist_timeout))
-    engine = FullyShardedEngine() if args.parallel == "fsdp" else DataParallelEngine()
+    if args.parallel == "pp":
+        from ..parallel.pipeline import PipelineEngine
+
+        engine = PipelineEngine()
+    else:
+        engine = FullyShardedEngine() if args.parallel == "fsdp" else DataParallelEngine()
     hb = None
     beat, check = store_client(), store_client()
     if beat is not None and check is not None:
@@ -207,8 +213,12 @@ def run(args) -> dict:
 
         enable_wavefront(model, args.wavefront)
     ds, eval_ds = split_eval(args, build_dataset(args, cfg.vocab_size), cfg.vocab_size)
-    # context parallel: every rank reads the same whole sequences and keeps its shard of them
-    dworld, drank = (1, 0) if cp is not None else (world, rank)
+    # context parallel: every rank reads the same whole sequences and keeps its shard of them;
+    # pipeline: every rank reads the same batches (stage 0 embeds them, the last stage scores them)
+    pp = args.parallel == "pp" and world > 1
+    if pp and args.model != "mac":
+        raise SystemExit("--parallel pp is for --model mac")
+    dworld, drank = (1, 0) if (cp is not None or pp) else (world, rank)
     sampler = DistributedSampler(ds, dworld, drank, shuffle=True, seed=args.seed) if (
         world > 1 and hasattr(ds, "__len__")) else None
     loader = DataLoader(ds, batch_size=args.batch_size, shuffle=(sampler is None and hasattr(ds, "__len__")),
@@ -229,7 +239,7 @@ def run(args) -> dict:
     dtype = {"bf16": torch.bfloat16, "none": torch.float32}[args.mixed_precision]
     graph = False
     if args.torch_compile:
-        graph = device.type == "cuda" and args.gradient_accumulation_steps == 1 and cp is None
+        graph = device.type == "cuda" and args.gradient_accumulation_steps == 1 and cp is None and not pp
         log.info("--torch-compile (%s): %s", args.compile_mode,
                  "whole-step CUDA-graph capture and replay" if graph else
                  "no CUDA graph (needs a CUDA device, no gradient accumulation and no context "

@@ -79,13 +79,15 @@ class MACPipeline:
         cs = self.model.config.chunk_size
         return [(s, min(cs, T - s)) for s in range(0, T, cs)]
 
-    def forward_backward(self, input_ids: torch.Tensor, labels: torch.Tensor | None = None, states=None):
+    def forward_backward(self, input_ids: torch.Tensor, labels: torch.Tensor | None = None, states=None,
+                         loss_scale: float = 1.0):
         """One pipelined forward (and, with ``labels``, backward) of a batch.
 
         Every rank passes the same ``input_ids`` (stage 0 embeds them) and
         ``labels`` (the last stage's loss).  Returns ``(loss, states)``: the mean
         loss on every rank (a detached scalar) and this stage's new memory
-        states.
+        states.  ``loss_scale`` scales the back-propagated loss (gradient
+        accumulation), not the returned value.
         """
         m = self.model
         blocks = m.blocks[self.lo:self.hi]
@@ -126,7 +128,7 @@ class MACPipeline:
                 part = cross_entropy(linear(m.norm(outs[c]), m.head.weight, use_kernels=uk), lab,
                                      use_kernels=uk) * (cnt / total)
                 if train:
-                    part.backward()
+                    (part * loss_scale if loss_scale != 1.0 else part).backward()
                     if not self.first:
                         self._send_grad(ins[c])
                 loss += part.detach().float()
@@ -164,6 +166,21 @@ class MACPipeline:
         optimizer.zero_grad()
         return loss
 
+    def sync_parameters(self) -> None:
+        """Bring every rank's copy of every stage's parameters up to date (each
+        stage's owner broadcasts them), e.g. before a checkpoint is written."""
+        if self.world == 1:
+            return
+        m = self.model
+        g = (lambda r: r) if self.group is None else (lambda r: dist.get_global_rank(self.group, r))
+        with torch.no_grad():
+            for s, (lo, hi) in enumerate(split_layers(len(m.blocks), self.world)):
+                for p in (q for b in m.blocks[lo:hi] for q in b.parameters()):
+                    dist.broadcast(p.data, src=g(s), group=self.group)
+            for p in m.norm.parameters():
+                dist.broadcast(p.data, src=g(self.world - 1), group=self.group)
+            dist.broadcast(m.embed.weight.data, src=g(0), group=self.group)
+
     def _send_grad(self, x: torch.Tensor) -> None:
         g = x.grad if x.grad is not None else torch.zeros_like(x)
         dist.send(g.contiguous(), dst=self.prev, group=self.group)
@@ -200,4 +217,44 @@ class MACPipeline:
         return norm
 
 
-__all__ = ["MACPipeline", "split_layers"]
+class PipelineEngine:
+    """Training engine for :class:`~titans_pytorch_b200.train.trainer.Trainer`
+    that runs a MAC model as a pipeline over the ranks of ``group``: the
+    trainer hands it each batch (the same batch on every rank), it runs the
+    pipelined forward and backward, clips over the stages and steps this
+    stage's AdamW.  Checkpoints gather every stage's parameters into the
+    unsharded model file and keep one optimizer file per stage."""
+
+    graph_safe = False
+
+    def __init__(self, group=None) -> None:
+        self.group = group
+        self.pipe: MACPipeline | None = None
+        self.clip = 0.0
+
+    def make_optimizer(self, model, cfg):
+        from ..train.optim import FusedAdamW
+
+        self.pipe = MACPipeline(model, self.group)
+        self.clip = float(cfg.grad_clip)
+        opt = FusedAdamW(self.pipe.parameters(), lr=cfg.lr, betas=cfg.betas, eps=cfg.eps,
+                         weight_decay=cfg.weight_decay, max_grad_norm=0.0,
+                         use_kernels=getattr(model.config, "use_kernels", None))
+        opt.shard_state = self.pipe.world > 1  # one optimizer file per stage
+
+        def full_model_state_dict(m):
+            self.pipe.sync_parameters()
+            return m.state_dict()
+
+        opt.full_model_state_dict = full_model_state_dict
+        return opt
+
+    def forward_backward(self, input_ids, labels, loss_scale: float = 1.0) -> torch.Tensor:
+        return self.pipe.forward_backward(input_ids, labels, loss_scale=loss_scale)[0]
+
+    def reduce_gradients(self, optimizer) -> None:
+        if self.clip > 0:
+            self.pipe.clip_grad_norm_(self.clip)
+
+
+__all__ = ["MACPipeline", "PipelineEngine", "split_layers"]

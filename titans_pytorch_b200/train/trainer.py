@@ -90,6 +90,9 @@ class Trainer:
         if self.cfg.cuda_graph:
             if self.device.type != "cuda" or self.cfg.gradient_accumulation_steps != 1:
                 raise ValueError("cuda_graph needs a CUDA device and no gradient accumulation")
+            if getattr(engine, "forward_backward", None) is not None:
+                raise ValueError("cuda_graph does not capture an engine that runs its own forward and "
+                                 "backward (pipeline stages)")
             if not getattr(self.optimizer, "graph_safe", False):
                 raise ValueError("cuda_graph needs a graph-safe optimizer (fused kernels; the fused "
                                  "data-parallel engine, not the collective one)")
@@ -113,11 +116,15 @@ class Trainer:
         ids = self._to_device(batch["input_ids"])
         labels = self._to_device(batch["labels"])
         accum = self.cfg.gradient_accumulation_steps
-        loss = self.loss_fn(ids, labels)
-        prep = getattr(self.optimizer, "prepare_backward", None)
-        if prep is not None:  # engines that reduce during the backward: is this the step's last one?
-            prep((self._micro + 1) % accum == 0)
-        self._backward(loss / accum if accum > 1 else loss)
+        fb = getattr(self.engine, "forward_backward", None)
+        if fb is not None:  # an engine that runs the forward and backward itself (pipeline stages)
+            loss = fb(ids, labels, loss_scale=1.0 / accum)
+        else:
+            loss = self.loss_fn(ids, labels)
+            prep = getattr(self.optimizer, "prepare_backward", None)
+            if prep is not None:  # engines that reduce during the backward: is this the step's last one?
+                prep((self._micro + 1) % accum == 0)
+            self._backward(loss / accum if accum > 1 else loss)
         self._micro += 1
         if self._micro % accum == 0:
             self.optimizer_step()
@@ -210,8 +217,12 @@ class Trainer:
                 break
             ids = self._to_device(b["input_ids"])
             labels = self._to_device(b["labels"])
-            logits, _ = self.model(ids)
-            loss = cross_entropy(logits, labels, use_kernels=getattr(self.model.config, "use_kernels", None))
+            fb = getattr(self.engine, "forward_backward", None)
+            if fb is not None:  # pipeline stages: the pipelined forward's loss (same on every rank)
+                loss = fb(ids, labels)
+            else:
+                logits, _ = self.model(ids)
+                loss = cross_entropy(logits, labels, use_kernels=getattr(self.model.config, "use_kernels", None))
             k = (labels != -100).sum()
             acc[0] += loss.double() * k
             acc[1] += k

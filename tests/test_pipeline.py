@@ -145,3 +145,45 @@ def test_mac_pipeline_training_matches_one_process(tmp_path):
             # difference in a gradient near zero can move a weight by a small fraction
             # of the step size (1e-3); a missing clip or tied-weight sum moves far more.
             torch.testing.assert_close(p, ref[n].detach(), atol=2e-4, rtol=0, msg=n)
+
+
+def _gpu_pp_worker(rank, world, out_dir):
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        fields = {**FIELDS, "dim": 256, "num_heads": 4, "chunk_size": 128, "window_size": 128, "vocab_size": 512,
+                  "init_std": 0.05}
+        g = torch.Generator().manual_seed(7)
+        d = torch.randint(0, 512, (2, 513), generator=g)
+        ids, lab = d[:, :-1].cuda(), d[:, 1:].cuda()
+        torch.manual_seed(0)
+        ref = T.TitansMAC(T.TitansConfig(**fields)).cuda().to(torch.bfloat16)
+        torch.manual_seed(0)
+        model = T.TitansMAC(T.TitansConfig(**fields)).cuda().to(torch.bfloat16)
+        loss_ref = cross_entropy(ref(ids)[0], lab)
+        loss_ref.backward()
+        pipe = MACPipeline(model)
+        loss, _ = pipe.forward_backward(ids, lab)
+        rg = dict(ref.named_parameters())
+        names = {p: n for n, p in model.named_parameters()}
+        worst = 0.0
+        for p in pipe.parameters():
+            a, b = p.grad.float(), rg[names[p]].grad.float()
+            worst = max(worst, ((a - b).norm() / b.norm().clamp_min(1e-12)).item())
+        torch.save({"loss": float(loss), "loss_ref": float(loss_ref), "worst": worst},
+                   os.path.join(out_dir, f"g{rank}.pt"))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_gpu_mac_pipeline_two_ranks(tmp_path):
+    """Two NCCL stages on bf16 kernels against the one-GPU model: the loss and each
+    stage's gradients (relative norm error of bf16 rounding)."""
+    run_workers(_gpu_pp_worker, 2, (str(tmp_path),), timeout=300)
+    for r in range(2):
+        res = torch.load(tmp_path / f"g{r}.pt")
+        assert abs(res["loss"] - res["loss_ref"]) < 2e-2 * abs(res["loss_ref"]), res
+        assert res["worst"] < 0.05, res

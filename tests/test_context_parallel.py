@@ -215,3 +215,48 @@ def test_gpu_context_parallel_two_ranks(tmp_path, cls):
         res = torch.load(tmp_path / f"g{r}.pt")
         assert res["err"] <= 0.05 * res["scale"] + 0.05, res
         assert res["state_err"] < 0.02, res
+
+
+def _cp_dp_worker(rank, world, out_dir, S):
+    """Four ranks: context-parallel pairs {0, 1} and {2, 3}, each pair on its own sequence."""
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    groups = [dist.new_group([0, 1]), dist.new_group([2, 3])]
+    torch.manual_seed(0)
+    model = T.TitansMAG(T.TitansConfig(**FIELDS, use_kernels=False))
+    shard = enable_context_parallel(model, groups[rank // 2])
+    assert (shard.rank, shard.world) == (rank % 2, 2)
+    ids, lab = (t[rank // 2:rank // 2 + 1] for t in (_batch(2, S, seed=9)["input_ids"],
+                                                    _batch(2, S, seed=9)["labels"]))
+    part = shard_batch({"input_ids": ids, "labels": lab}, shard)
+    logits, _ = model(part["input_ids"])
+    cross_entropy(logits, part["labels"]).backward()
+    grads = {}
+    for n, p in model.named_parameters():
+        if p.grad is not None:
+            g = p.grad.detach().clone()
+            dist.all_reduce(g)  # the data-parallel average over all four ranks
+            grads[n] = g / world
+    torch.save(grads, os.path.join(out_dir, f"cpdp{rank}.pt"))
+    dist.destroy_process_group()
+
+
+def test_context_parallel_inside_data_parallel(tmp_path):
+    """Two data-parallel replicas, each a context-parallel pair: the gradients averaged
+    over all ranks equal the mean of the two sequences' whole-sequence gradients."""
+    S = 32
+    run_workers(_cp_dp_worker, 4, (str(tmp_path), S))
+    b = _batch(2, S, seed=9)
+    ref = {}
+    for i in range(2):
+        torch.manual_seed(0)
+        model = T.TitansMAG(T.TitansConfig(**FIELDS, use_kernels=False))
+        logits, _ = model(b["input_ids"][i:i + 1])
+        cross_entropy(logits, b["labels"][i:i + 1]).backward()
+        for n, p in model.named_parameters():
+            if p.grad is not None:
+                ref[n] = ref.get(n, 0) + p.grad / 2
+    for r in range(4):
+        got = torch.load(tmp_path / f"cpdp{r}.pt")
+        assert got.keys() == ref.keys()
+        for n, g in ref.items():
+            torch.testing.assert_close(got[n], g, atol=2e-6, rtol=1e-3, msg=n)

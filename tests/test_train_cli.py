@@ -68,6 +68,19 @@ def test_context_parallel_cli(tmp_path):
     assert (ck / "final_model.pt").exists()
 
 
+def test_context_parallel_cli_groups(tmp_path):
+    """--parallel cp --cp-size 2 on four gloo ranks: two data-parallel replicas of a
+    context-parallel pair."""
+    ck, mf = tmp_path / "ck", tmp_path / "m.jsonl"
+    argv = COMMON + ["--parallel", "cp", "--cp-size", "2", "--max-steps", "2", "--eval-every", "0",
+                     "--save-every", "0", "--checkpoint-dir", str(ck), "--metrics-file", str(mf),
+                     "--heartbeat-timeout", "30", "--dist-timeout", "60"]
+    run_workers(_rank_main, 4, (argv,), timeout=240)
+    lines = [json.loads(x) for x in mf.read_text().splitlines()]
+    assert [x["step"] for x in lines if "train/loss" in x] == [1, 2]
+    assert (ck / "final_model.pt").exists()
+
+
 def test_pipeline_cli_resume(tmp_path):
     """--parallel pp (MAC over two gloo stages): the checkpoint gathers both stages'
     weights into the model file, keeps one optimizer file per stage, and resuming

@@ -108,6 +108,9 @@ def build_parser() -> argparse.ArgumentParser:
     a("--compile-mode", type=str, default="reduce-overhead",
       help="with --torch-compile: reduce-overhead / max-autotune / default all mean CUDA-graph replay")
     a("--gradient-checkpointing", action="store_true")
+    a("--cp-size", type=int, default=0,
+      help="--parallel cp: ranks per context-parallel group (default: all ranks); the groups are data-parallel "
+           "replicas of each other")
     a("--wavefront", type=int, default=0,
       help="MAC: run the (layer, segment) loop as a wavefront on this many CUDA streams (0 = sequential; "
            "not with --parallel fsdp)")
@@ -200,12 +203,19 @@ def run(args) -> dict:
     cfg = TitansConfig(**fields)
     model = create_model(args.model, cfg)
     cp = None
+    cps = 1
     if args.parallel == "cp" and world > 1:
+        import torch.distributed as dist
+
         from ..parallel.context import enable_context_parallel
 
-        cp = enable_context_parallel(model)
-        if args.seq_len % world:
-            raise SystemExit(f"--parallel cp: --seq-len {args.seq_len} must be divisible by {world} ranks")
+        cps = args.cp_size or world
+        if world % cps or args.seq_len % cps:
+            raise SystemExit(f"--parallel cp: --cp-size {cps} must divide the {world} ranks and --seq-len "
+                             f"{args.seq_len}")
+        # every rank creates every group, in the same order
+        groups = [dist.new_group(list(range(g * cps, (g + 1) * cps))) for g in range(world // cps)]
+        cp = enable_context_parallel(model, groups[rank // cps] if cps < world else None)
     if args.gradient_checkpointing:
         enable_gradient_checkpointing(model)
     if args.wavefront > 1 and args.model == "mac" and device.type == "cuda":
@@ -218,7 +228,7 @@ def run(args) -> dict:
     pp = args.parallel == "pp" and world > 1
     if pp and args.model != "mac":
         raise SystemExit("--parallel pp is for --model mac")
-    dworld, drank = (1, 0) if (cp is not None or pp) else (world, rank)
+    dworld, drank = (1, 0) if pp else ((world // cps, rank // cps) if cp is not None else (world, rank))
     sampler = DistributedSampler(ds, dworld, drank, shuffle=True, seed=args.seed) if (
         world > 1 and hasattr(ds, "__len__")) else None
     loader = DataLoader(ds, batch_size=args.batch_size, shuffle=(sampler is None and hasattr(ds, "__len__")),

@@ -90,6 +90,9 @@ class Trainer:
         if self.cfg.cuda_graph:
             if self.device.type != "cuda" or self.cfg.gradient_accumulation_steps != 1:
                 raise ValueError("cuda_graph needs a CUDA device and no gradient accumulation")
+            if any(getattr(getattr(b, "cp", None), "active", False) for b in getattr(self.model, "blocks", ())):
+                raise ValueError("cuda_graph does not capture context parallelism (its halo exchange and "
+                                 "memory all-reduce are host-issued point-to-point calls)")
             if getattr(engine, "forward_backward", None) is not None:
                 raise ValueError("cuda_graph does not capture an engine that runs its own forward and "
                                  "backward (pipeline stages)")

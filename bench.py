@@ -331,8 +331,8 @@ def main():
                          "parameters kept until the step)")
     ap.add_argument("--wavefront", type=int, default=-1,
                     help="mac400m: run the (layer, segment) loop as a wavefront on this many CUDA streams "
-                         "(0 = sequential; default: 2 where the gradients are reduced after the backward, "
-                         "i.e. one GPU or dp without overlap)")
+                         "(0 = sequential; default: 2 on one GPU, 0 with several; dp without overlap also "
+                         "takes it, fsdp does not)")
     args = ap.parse_args()
     global CFG, MODEL_FIELDS, SEQ, MICRO_BATCH
     CFG = CONFIGS[args.config]
@@ -357,7 +357,7 @@ def main():
     else:
         overlap = args.overlap == "on" or (args.overlap == "auto" and args.parallel == "fsdp")
         if args.wavefront < 0:
-            args.wavefront = 2 if world == 1 or (args.parallel == "dp" and not overlap) else 0
+            args.wavefront = 2 if world == 1 else 0  # measured on one GPU; ask for it explicitly with dp
         trainer, nparams = build_ours(device, world, args.parallel, overlap=overlap,
                                       reshard=args.fsdp_mode == "full", wavefront=args.wavefront)
         prefixes = ("tb::",)

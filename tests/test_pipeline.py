@@ -187,3 +187,40 @@ def test_gpu_mac_pipeline_two_ranks(tmp_path):
         res = torch.load(tmp_path / f"g{r}.pt")
         assert abs(res["loss"] - res["loss_ref"]) < 2e-2 * abs(res["loss_ref"]), res
         assert res["worst"] < 0.05, res
+
+
+def _pp_engine_worker(rank, world, out_dir):
+    from titans_pytorch_b200.parallel.pipeline import PipelineEngine
+    from titans_pytorch_b200.train.trainer import Trainer, TrainStepConfig
+
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    torch.manual_seed(0)
+    model = T.TitansMAC(T.TitansConfig(**FIELDS, use_kernels=False))
+    names = {p: n for n, p in model.named_parameters()}
+    cfg = TrainStepConfig(lr=1e-3, dtype=torch.float32, gradient_accumulation_steps=2, grad_clip=0.5)
+    tr = Trainer(model, cfg, device="cpu", engine=PipelineEngine())
+    for seed in range(4):  # two optimizer steps of two micro-batches
+        ids, lab = _batch(2, 24, seed=seed)
+        tr.train_step({"input_ids": ids, "labels": lab})
+    own = {names[p]: p.detach().clone() for p in tr.engine.pipe.parameters()}
+    torch.save(own, os.path.join(out_dir, f"en{rank}.pt"))
+    dist.destroy_process_group()
+
+
+def test_pipeline_engine_gradient_accumulation(tmp_path):
+    """The Trainer with PipelineEngine and two accumulated micro-batches per step equals
+    the one-process Trainer (the tied weight's gradient is summed once per step)."""
+    from titans_pytorch_b200.train.trainer import Trainer, TrainStepConfig
+
+    run_workers(_pp_engine_worker, 2, (str(tmp_path),))
+    torch.manual_seed(0)
+    model = T.TitansMAC(T.TitansConfig(**FIELDS, use_kernels=False))
+    cfg = TrainStepConfig(lr=1e-3, dtype=torch.float32, gradient_accumulation_steps=2, grad_clip=0.5)
+    tr = Trainer(model, cfg, device="cpu")
+    for seed in range(4):
+        ids, lab = _batch(2, 24, seed=seed)
+        tr.train_step({"input_ids": ids, "labels": lab})
+    ref = dict(model.named_parameters())
+    for r in range(2):
+        for n, p in torch.load(tmp_path / f"en{r}.pt").items():
+            torch.testing.assert_close(p, ref[n].detach(), atol=2e-4, rtol=0, msg=n)

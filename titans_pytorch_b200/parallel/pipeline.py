@@ -80,14 +80,16 @@ class MACPipeline:
         return [(s, min(cs, T - s)) for s in range(0, T, cs)]
 
     def forward_backward(self, input_ids: torch.Tensor, labels: torch.Tensor | None = None, states=None,
-                         loss_scale: float = 1.0):
+                         loss_scale: float = 1.0, sync_tied: bool = True):
         """One pipelined forward (and, with ``labels``, backward) of a batch.
 
         Every rank passes the same ``input_ids`` (stage 0 embeds them) and
         ``labels`` (the last stage's loss).  Returns ``(loss, states)``: the mean
         loss on every rank (a detached scalar) and this stage's new memory
         states.  ``loss_scale`` scales the back-propagated loss (gradient
-        accumulation), not the returned value.
+        accumulation), not the returned value.  ``sync_tied=False`` leaves the
+        tied weight's gradient unsummed (call :meth:`sync_tied_grads` once after
+        the last accumulated micro-batch).
         """
         m = self.model
         blocks = m.blocks[self.lo:self.hi]
@@ -142,7 +144,7 @@ class MACPipeline:
         if labels is not None and self.world > 1:
             dist.broadcast(loss, src=self.world - 1 if self.group is None else dist.get_global_rank(
                 self.group, self.world - 1), group=self.group)
-        if train:
+        if train and sync_tied:
             self.sync_tied_grads()
         return loss, states
 
@@ -250,9 +252,11 @@ class PipelineEngine:
         return opt
 
     def forward_backward(self, input_ids, labels, loss_scale: float = 1.0) -> torch.Tensor:
-        return self.pipe.forward_backward(input_ids, labels, loss_scale=loss_scale)[0]
+        # the tied weight's gradient is summed once per optimizer step, in reduce_gradients
+        return self.pipe.forward_backward(input_ids, labels, loss_scale=loss_scale, sync_tied=False)[0]
 
     def reduce_gradients(self, optimizer) -> None:
+        self.pipe.sync_tied_grads()
         if self.clip > 0:
             self.pipe.clip_grad_norm_(self.clip)
 
